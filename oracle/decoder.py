@@ -26,6 +26,13 @@ import numpy as np
 ACC = np.float64
 
 
+def set_precision(dtype):
+    """Arithmetic type of every oracle function (float64 for checking, float32 to time
+    the reference's float32 arithmetic)."""
+    global ACC
+    ACC = np.dtype(dtype).type
+
+
 # --------------------------------------------------------------------------------------
 # Elementwise pieces
 # --------------------------------------------------------------------------------------
@@ -56,21 +63,21 @@ def apply_rope(x: np.ndarray, positions: np.ndarray, cos: np.ndarray, sin: np.nd
     hd = x.shape[-1]
     c = cos[positions][..., None, :].astype(ACC)
     s = sin[positions][..., None, :].astype(ACC)
-    x = x.astype(ACC)
+    x = np.asarray(x, dtype=ACC)
     rot = np.concatenate([-x[..., hd // 2:], x[..., : hd // 2]], axis=-1)
     return x * c + rot * s
 
 
 def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     """engine/tensor_parallel/layers.py:179-184: ``x * rsqrt(mean(x^2) + eps) * w``."""
-    x = x.astype(ACC)
+    x = np.asarray(x, dtype=ACC)
     var = np.mean(x * x, axis=-1, keepdims=True)
-    return x / np.sqrt(var + eps) * w.astype(ACC)
+    return x / np.sqrt(var + eps) * np.asarray(w, dtype=ACC)
 
 
 def silu(x: np.ndarray) -> np.ndarray:
     """torch.nn.functional.silu as used at engine/model/mlp.py:82."""
-    x = x.astype(ACC)
+    x = np.asarray(x, dtype=ACC)
     return x / (1.0 + np.exp(-x))
 
 
@@ -82,9 +89,9 @@ def softmax(s: np.ndarray, axis: int = -1) -> np.ndarray:
 
 def column_parallel_linear(x: np.ndarray, w_in_out: np.ndarray, bias: Optional[np.ndarray] = None):
     """engine/tensor_parallel/layers.py:78-86: ``Y = X @ W (+ b)`` with W stored [in, out/t]."""
-    y = x.astype(ACC) @ w_in_out.astype(ACC)
+    y = np.asarray(x, dtype=ACC) @ np.asarray(w_in_out, dtype=ACC)
     if bias is not None:
-        y = y + bias.astype(ACC)
+        y = y + np.asarray(bias, dtype=ACC)
     return y
 
 
@@ -98,7 +105,7 @@ def all_reduce_sum(partials: Sequence[np.ndarray]) -> np.ndarray:
 
 def row_parallel_linear(xs: Sequence[np.ndarray], ws: Sequence[np.ndarray], bias=None):
     """engine/tensor_parallel/layers.py:147-162: per-rank partial ``X_r @ W_r``, all-reduce, ``+b``."""
-    out = all_reduce_sum([x.astype(ACC) @ w.astype(ACC) for x, w in zip(xs, ws)])
+    out = all_reduce_sum([np.asarray(x, dtype=ACC) @ np.asarray(w, dtype=ACC) for x, w in zip(xs, ws)])
     if bias is not None:
         out = out + bias
     return out
@@ -201,15 +208,15 @@ def decode_attention(q, k_new, v_new, positions, pool: KVPool, layer, block_tabl
         blk, off = physical_slot(block_tables[b], pos, bs)
         pool.store(layer, blk, off, k_new[b], v_new[b])
         k_seq, v_seq = pool.read_sequence(layer, block_tables[b], pos + 1)
-        ks.append(k_seq.astype(ACC))
-        vs.append(v_seq.astype(ACC))
+        ks.append(np.asarray(k_seq, dtype=ACC))
+        vs.append(np.asarray(v_seq, dtype=ACC))
     max_len = max(k.shape[0] for k in ks)
     out = np.zeros((B, nq, hd), dtype=ACC)
     for b in range(B):
         ctx = ks[b].shape[0]
         for h in range(nq):
             g = h // rep  # repeat_kv, attention.py:66-76
-            s = (ks[b][:, g, :] @ q[b, h].astype(ACC)) * scale
+            s = (ks[b][:, g, :] @ np.asarray(q[b, h], dtype=ACC)) * scale
             if compat_pad and ctx < max_len:
                 s = np.concatenate([s, np.zeros(max_len - ctx, dtype=ACC)])
             p = softmax(s)
@@ -322,7 +329,7 @@ class OracleModel:
             assert S == 1
             a = decode_attention(q[:, 0], k[:, 0], v[:, 0], positions[:, 0], self.pools[r], layer,
                                  block_tables, scale, self.compat_pad)[:, None, :]
-        return a @ w[pre + "out_proj.weight"].astype(ACC)
+        return a @ np.asarray(w[pre + "out_proj.weight"], dtype=ACC)
 
     # engine/model/mlp.py:72-86 for one rank
     def _mlp_rank(self, r, layer, x):
@@ -330,7 +337,7 @@ class OracleModel:
         pre = f"layers.{layer}.mlp."
         g = column_parallel_linear(x, w[pre + "gate_proj.weight"])
         u = column_parallel_linear(x, w[pre + "up_proj.weight"])
-        return (silu(g) * u) @ w[pre + "down_proj.weight"].astype(ACC)
+        return (silu(g) * u) @ np.asarray(w[pre + "down_proj.weight"], dtype=ACC)
 
     def block(self, layer, h, positions, block_tables, is_prefill):
         """engine/model/llama.py:48-76 (pre-norm residual block)."""
@@ -350,14 +357,14 @@ class OracleModel:
         w0 = self.shards[0]
         token_ids = np.asarray(token_ids)
         positions = np.asarray(positions)
-        h = w0["embed_tokens.weight"][token_ids].astype(ACC)
+        h = np.asarray(w0["embed_tokens.weight"][token_ids], dtype=ACC)
         for layer in range(self.cfg.num_layers):
             h = self.block(layer, h, positions, block_tables, is_prefill)
             if trace is not None:
                 trace.append(h.copy())
         h = rmsnorm(h, w0["norm.weight"], self.cfg.rms_norm_eps)
         hl = h[:, -1, :] if last_only else h
-        return hl @ w0["lm_head.weight"].astype(ACC).T
+        return hl @ np.asarray(w0["lm_head.weight"], dtype=ACC).T
 
 
 # --------------------------------------------------------------------------------------

@@ -1,0 +1,121 @@
+// Shared helpers for the libb2tp kernels: status handling, dtype conversion,
+// vector loads, warp reductions and bounded waits.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "b2tp.h"
+
+namespace b2 {
+
+// Records a formatted message as the calling thread's last error and returns `status`.
+int fail(int status, const char* fmt, ...);
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+#define B2_TRY_CUDA(expr)                                                                  \
+  do {                                                                                     \
+    cudaError_t e_ = (expr);                                                               \
+    if (e_ != cudaSuccess)                                                                 \
+      return ::b2::fail(B2_ECUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), \
+                        __FILE__, __LINE__);                                               \
+  } while (0)
+
+#define B2_CHECK_ARG(cond, ...)                           \
+  do {                                                    \
+    if (!(cond)) return ::b2::fail(B2_EINVAL, __VA_ARGS__); \
+  } while (0)
+
+inline bool valid_dtype(int d) { return d == B2_F32 || d == B2_BF16; }
+inline size_t dtype_bytes(int d) { return d == B2_BF16 ? 2 : 4; }
+
+// ------------------------------------------------------------------ conversions
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Runtime-typed scalar access for the small memory-bound kernels.
+__device__ __forceinline__ float ld_dyn(const void* p, int dtype, size_t i) {
+  return dtype == B2_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i])
+                          : reinterpret_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ void st_dyn(void* p, int dtype, size_t i, float v) {
+  if (dtype == B2_BF16)
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else
+    reinterpret_cast<float*>(p)[i] = v;
+}
+
+// 16-byte vector of T converted to float.
+template <typename T>
+struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+};
+
+template <typename T>
+__device__ __forceinline__ void load16_f32(const T* p, float (&out)[16 / sizeof(T)]) {
+  uint4 raw = *reinterpret_cast<const uint4*>(p);
+  if constexpr (sizeof(T) == 4) {
+    out[0] = __uint_as_float(raw.x);
+    out[1] = __uint_as_float(raw.y);
+    out[2] = __uint_as_float(raw.z);
+    out[3] = __uint_as_float(raw.w);
+  } else {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      out[2 * i] = __uint_as_float(w[i] << 16);
+      out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ reductions
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum for blockDim.x a multiple of 32 (<= 1024); `red` holds >= 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = (threadIdx.x < nw) ? red[threadIdx.x] : 0.f;
+  if (warp == 0) t = warp_sum(t);
+  if (threadIdx.x == 0) red[0] = t;
+  __syncthreads();
+  return red[0];
+}
+
+__device__ __forceinline__ void raise_status(int32_t* status, int bits) {
+  if (status) atomicOr(reinterpret_cast<int*>(status), bits);
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+}  // namespace b2

@@ -1,0 +1,76 @@
+// C-ABI entry points of the linear layers.  bf16 runs on the tcgen05 kernel
+// (gemm_tc.cu), float32 on the FFMA kernel (gemm_simt.cu).
+#include "gemm.cuh"
+
+namespace b2 {
+
+static int check_common(const void* x, int M, int K, int N, int dtype, int y_dtype, const char* who) {
+  B2_CHECK_ARG(M >= 0 && K > 0 && N > 0, "%s: bad sizes M=%d K=%d N=%d", who, M, K, N);
+  B2_CHECK_ARG(valid_dtype(dtype) && valid_dtype(y_dtype), "%s: bad dtype", who);
+  B2_CHECK_ARG(M == 0 || x, "%s: null input", who);
+  return B2_OK;
+}
+
+}  // namespace b2
+
+extern "C" {
+
+size_t b2_linear_workspace_bytes(int M, int N, int K, int dtype) {
+  if (dtype != B2_BF16 || M <= 0 || N <= 0 || K <= 0) return 0;
+  size_t a = b2::gemm_tc_workspace_bytes(M, N, K, b2::kEpiStore);
+  size_t b = b2::gemm_tc_workspace_bytes(M, N, K, b2::kEpiSwiglu);
+  return a > b ? a : b;
+}
+
+int b2_linear(const void* x, int64_t ldx, int M, int K, const void* w, int N, const float* bias,
+              void* y, int64_t ldy, int dtype, int y_dtype, void* workspace, size_t workspace_bytes,
+              int32_t* status, b2_stream_t stream) {
+  int rc = b2::check_common(x, M, K, N, dtype, y_dtype, "b2_linear");
+  if (rc) return rc;
+  B2_CHECK_ARG(ldx >= K && ldy >= N, "b2_linear: row strides too small");
+  if (M == 0) return B2_OK;
+  B2_CHECK_ARG(w && y, "b2_linear: null pointer");
+  if (dtype == B2_F32) return b2::gemm_simt(x, ldx, M, K, w, nullptr, N, bias, y, ldy, dtype, y_dtype, stream);
+  b2::GemmSeg seg{w, N, 0};
+  return b2::gemm_tc(x, ldx, M, K, &seg, 1, b2::kEpiStore, bias, y, ldy, y_dtype, workspace, workspace_bytes,
+                     status, stream);
+}
+
+int b2_linear_qkv(const void* x, int64_t ldx, int M, int K, const void* wq, int Nq, const void* wk,
+                  int Nk, const void* wv, int Nv, void* y, int64_t ldy, int dtype, void* workspace,
+                  size_t workspace_bytes, int32_t* status, b2_stream_t stream) {
+  int rc = b2::check_common(x, M, K, Nq + Nk + Nv, dtype, dtype, "b2_linear_qkv");
+  if (rc) return rc;
+  B2_CHECK_ARG(Nq > 0 && Nk > 0 && Nv > 0, "b2_linear_qkv: bad segment sizes");
+  B2_CHECK_ARG(ldx >= K && ldy >= (int64_t)Nq + Nk + Nv, "b2_linear_qkv: row strides too small");
+  if (M == 0) return B2_OK;
+  B2_CHECK_ARG(wq && wk && wv && y, "b2_linear_qkv: null pointer");
+  const size_t esz = b2::dtype_bytes(dtype);
+  if (dtype == B2_F32) {
+    char* yb = static_cast<char*>(y);
+    rc = b2::gemm_simt(x, ldx, M, K, wq, nullptr, Nq, nullptr, yb, ldy, dtype, dtype, stream);
+    if (rc) return rc;
+    rc = b2::gemm_simt(x, ldx, M, K, wk, nullptr, Nk, nullptr, yb + esz * Nq, ldy, dtype, dtype, stream);
+    if (rc) return rc;
+    return b2::gemm_simt(x, ldx, M, K, wv, nullptr, Nv, nullptr, yb + esz * (Nq + Nk), ldy, dtype, dtype, stream);
+  }
+  b2::GemmSeg segs[3] = {{wq, Nq, 0}, {wk, Nk, Nq}, {wv, Nv, Nq + Nk}};
+  return b2::gemm_tc(x, ldx, M, K, segs, 3, b2::kEpiStore, nullptr, y, ldy, dtype, workspace, workspace_bytes,
+                     status, stream);
+}
+
+int b2_linear_swiglu(const void* x, int64_t ldx, int M, int K, const void* w_gate, const void* w_up,
+                     int N, void* y, int64_t ldy, int dtype, void* workspace,
+                     size_t workspace_bytes, int32_t* status, b2_stream_t stream) {
+  int rc = b2::check_common(x, M, K, N, dtype, dtype, "b2_linear_swiglu");
+  if (rc) return rc;
+  B2_CHECK_ARG(ldx >= K && ldy >= N, "b2_linear_swiglu: row strides too small");
+  if (M == 0) return B2_OK;
+  B2_CHECK_ARG(w_gate && w_up && y, "b2_linear_swiglu: null pointer");
+  if (dtype == B2_F32) return b2::gemm_simt(x, ldx, M, K, w_gate, w_up, N, nullptr, y, ldy, dtype, dtype, stream);
+  b2::GemmSeg segs[2] = {{w_gate, N, 0}, {w_up, N, 0}};
+  return b2::gemm_tc(x, ldx, M, K, segs, 2, b2::kEpiSwiglu, nullptr, y, ldy, dtype, workspace, workspace_bytes,
+                     status, stream);
+}
+
+}  // extern "C"

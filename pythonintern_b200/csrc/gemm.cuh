@@ -1,0 +1,33 @@
+// Internal declarations shared by the GEMM translation units.
+#pragma once
+#include "common.cuh"
+
+namespace b2 {
+
+// silu(x) = x / (1 + exp(-x)), float32 (torch.nn.functional.silu, engine/model/mlp.py:82)
+__device__ __forceinline__ float silu_f32(float x) { return x / (1.f + expf(-x)); }
+
+// Epilogue kinds of the tensor-core GEMM.
+enum GemmEpi { kEpiStore = 0, kEpiSwiglu = 1 };
+
+// One output segment of a grouped launch: rows [0, n) of the packed [n, K] weight w,
+// written to output columns [col_off, col_off + n).
+struct GemmSeg {
+  const void* w;
+  int n;
+  int col_off;
+};
+
+int gemm_simt(const void* x, int64_t ldx, int M, int K, const void* w0, const void* w1, int N,
+              const float* bias, void* y, int64_t ldy, int dtype, int y_dtype, cudaStream_t s);
+
+// bf16 tcgen05 GEMM. For kEpiStore: nseg segments (1..3) concatenated along N.
+// For kEpiSwiglu: segs[0] = gate, segs[1] = up, both with n = N.
+size_t gemm_tc_workspace_bytes(int M, int n_total, int K, int epi);
+int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int nseg, int epi,
+            const float* bias, void* y, int64_t ldy, int y_dtype, void* ws, size_t ws_bytes,
+            int32_t* status, cudaStream_t s);
+// Returns true when the tensor-core kernel supports the shape (K % 8 == 0, 16-byte aligned rows).
+bool gemm_tc_supported(const void* x, int64_t ldx, int K, const GemmSeg* segs, int nseg);
+
+}  // namespace b2

@@ -1,0 +1,161 @@
+"""Sharded LLaMA / Mistral decoder (engine/model/llama.py:25-174).
+
+``DistributedTransformerBlock`` and ``DistributedLLaMAModel`` keep the reference's
+module tree and parameter names (so ``state_dict`` keys match the reference and
+its WeightSharder), and the reference's forward signatures.
+
+``DistributedLLaMAModel.forward`` runs the fused path: the residual stream stays
+float32 in HBM and each row-parallel projection is followed by ONE kernel that
+all-reduces (NVLink peer loads when world_size > 1), adds the residual and applies
+the NEXT RMSNorm (the post-attention norm, the next layer's input norm, or the
+final norm), so a decoder layer is seven kernels:
+
+    qkv GEMM -> RoPE + KV write -> paged attention -> o_proj GEMM
+    -> all-reduce + residual + norm -> gate/up GEMM + SwiGLU -> down GEMM
+    -> all-reduce + residual + norm
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional
+
+import torch
+import torch.nn as nn
+
+from pythonintern_b200 import kernels
+from pythonintern_b200.config import ModelConfig
+from pythonintern_b200.model.attention import DistributedAttention
+from pythonintern_b200.model.kv_cache import PhysicalKVCachePool
+from pythonintern_b200.model.metadata import TokenMetadata, build_metadata
+from pythonintern_b200.model.mlp import DistributedMLP
+from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
+from pythonintern_b200.tensor_parallel.layers import RMSNorm, RowParallelLinear
+from pythonintern_b200._lib import torch_dtype
+
+
+def _row_parallel_norm(proj: RowParallelLinear, inp: torch.Tensor, h: torch.Tensor, norm_w: torch.Tensor,
+                       eps: float, y: torch.Tensor, comm: Optional[DistributedCommunicator]):
+    """``h += AllReduce(inp @ W)``; ``y = rmsnorm(h) * norm_w`` (layers.py:147-162 + llama.py:70-75)."""
+    T, H = h.shape
+    wdt = proj.weight.dtype
+    if proj.world_size > 1 and comm is not None:
+        parity = comm.next_parity()
+        partial = comm.partial_buffer(parity, (T, H), wdt)
+        kernels.linear(inp, proj.packed_weight(), out=partial)
+        comm.allreduce_rmsnorm(parity, T, H, wdt, h, h, norm_w, eps, y)
+    else:
+        partial = kernels.linear(inp, proj.packed_weight())
+        kernels.rmsnorm(partial, norm_w, eps, residual=h, h_out=h, out=y)
+
+
+class DistributedTransformerBlock(nn.Module):
+    """Pre-norm residual block: ``h = x + attn(norm(x)); out = h + mlp(norm(h))`` (llama.py:25-76)."""
+
+    def __init__(self, config: ModelConfig, layer_idx: int, rank: int = 0, world_size: int = 1,
+                 communicator: Optional[DistributedCommunicator] = None, device=None):
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.input_layernorm = RMSNorm(config.hidden_dim, eps=config.rms_norm_eps, device=device)
+        self.self_attn = DistributedAttention(config, layer_idx, rank, world_size, communicator, device=device)
+        self.post_attention_layernorm = RMSNorm(config.hidden_dim, eps=config.rms_norm_eps, device=device)
+        self.mlp = DistributedMLP(config, layer_idx, rank, world_size, communicator, device=device)
+
+    def set_communicator(self, communicator: DistributedCommunicator):
+        self.self_attn.set_communicator(communicator)
+        self.mlp.set_communicator(communicator)
+
+    def forward(self, x: torch.Tensor, positions: torch.Tensor, kv_pool: Optional[PhysicalKVCachePool] = None,
+                block_tables: Optional[List[List[int]]] = None, is_prefill: bool = True,
+                step_id: int = 0) -> torch.Tensor:
+        with torch.no_grad():
+            B, S, H = x.shape
+            wdt = self.self_attn.q_proj.weight.dtype
+            h = x.reshape(B * S, H).to(torch.float32).contiguous()  # residual stream, float32
+            xn = kernels.rmsnorm(h, self.input_layernorm.weight, self.input_layernorm.eps, out_dtype=wdt)
+            attn = self.self_attn(xn.view(B, S, H), positions, kv_pool, block_tables, is_prefill, step_id)
+            xn2 = kernels.rmsnorm(attn, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps,
+                                  residual=h, h_out=h, out_dtype=wdt)
+            mlp = self.mlp(xn2.view(B, S, H), step_id=step_id)
+            kernels.residual_add(mlp, h)
+            return h.view(B, S, H).to(x.dtype)
+
+
+class DistributedLLaMAModel(nn.Module):
+    """Embedding, N blocks, final norm, replicated lm_head (llama.py:79-174)."""
+
+    def __init__(self, config: ModelConfig, rank: int = 0, world_size: int = 1,
+                 communicator: Optional[DistributedCommunicator] = None, device="cuda"):
+        super().__init__()
+        self.config = config
+        self.rank = rank
+        self.world_size = world_size
+        self.communicator = communicator
+        dev = torch.device(device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        if dev.type != "cuda":
+            raise ValueError("DistributedLLaMAModel runs on CUDA devices only")
+        self.device = dev
+        dt = torch_dtype(config.dtype)
+        self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_dim, device=dev, dtype=dt)
+        self.layers = nn.ModuleList([
+            DistributedTransformerBlock(config, i, rank, world_size, communicator, device=dev)
+            for i in range(config.num_layers)])
+        self.norm = RMSNorm(config.hidden_dim, eps=config.rms_norm_eps, device=dev)
+        self.lm_head = nn.Linear(config.hidden_dim, config.vocab_size, bias=False, device=dev, dtype=dt)
+
+    def set_communicator(self, communicator: DistributedCommunicator):
+        self.communicator = communicator
+        for layer in self.layers:
+            layer.set_communicator(communicator)
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.embed_tokens.weight.dtype
+
+    def forward_hidden(self, token_ids: torch.Tensor, md: TokenMetadata, kv_pool: PhysicalKVCachePool,
+                       trace: Optional[list] = None) -> torch.Tensor:
+        """Runs every layer; returns the final-normed hidden states [T, hidden] in the model dtype.
+
+        ``trace`` (optional list) receives a copy of the float32 residual stream after
+        each layer (the reference block's output), for parity checks.
+        """
+        cfg = self.config
+        eps = cfg.rms_norm_eps
+        T, H = md.n_tokens, cfg.hidden_dim
+        wdt = self.dtype
+        comm = self.communicator if self.world_size > 1 else None
+        ids = token_ids.reshape(-1)
+        if ids.device != self.device or ids.dtype != torch.int64:
+            ids = ids.to(self.device, torch.int64)
+        h = kernels.embedding(ids, self.embed_tokens.weight, out_dtype=torch.float32)
+        xn = torch.empty(T, H, dtype=wdt, device=self.device)
+        kernels.rmsnorm(h, self.layers[0].input_layernorm.weight, eps, out=xn)
+        n = len(self.layers)
+        for i, layer in enumerate(self.layers):
+            attn = layer.self_attn.attend(xn, md, kv_pool)
+            _row_parallel_norm(layer.self_attn.out_proj, attn, h, layer.post_attention_layernorm.weight, eps, xn,
+                               comm)
+            inter = layer.mlp.gate_up(xn)
+            next_w = self.layers[i + 1].input_layernorm.weight if i + 1 < n else self.norm.weight
+            _row_parallel_norm(layer.mlp.down_proj, inter, h, next_w, eps, xn, comm)
+            if trace is not None:
+                trace.append(h.clone())
+        return xn
+
+    def forward(self, token_ids: torch.Tensor, positions: torch.Tensor,
+                kv_pool: Optional[PhysicalKVCachePool] = None, block_tables: Optional[List[List[int]]] = None,
+                is_prefill: bool = True, step_id: int = 0, return_logits_last_only: bool = True,
+                metadata: Optional[TokenMetadata] = None, trace: Optional[list] = None) -> torch.Tensor:
+        """token_ids/positions: [batch, seq_len] -> float32 logits [batch, vocab] (last token) or [batch, seq, vocab]."""
+        if kv_pool is None or block_tables is None:
+            raise ValueError("the fused decoder path needs a KV pool and block tables")
+        with torch.no_grad():
+            B, S = token_ids.shape
+            md = metadata or build_metadata(positions, block_tables, is_prefill, self.device,
+                                            masked_padding=self.config.masked_decode_padding)
+            xn = self.forward_hidden(token_ids, md, kv_pool, trace=trace)
+            if return_logits_last_only:
+                last = xn.view(B, S, -1)[:, -1, :]  # row-strided view, no copy
+                return kernels.linear(last, self.lm_head.weight, out_dtype=torch.float32)
+            return kernels.linear(xn, self.lm_head.weight, out_dtype=torch.float32).view(B, S, -1)

@@ -1,0 +1,113 @@
+"""Worker step driver (engine/worker/execution_engine.py:24-160).
+
+``WorkerExecutionEngine(model_config, shard_config, kv_config, communicator,
+device).execute_step(step_request)`` keeps the reference's semantics: each
+prefill runs as its own batch-1 forward with positions ``arange(P)``; all decodes
+run as one batch with positions ``current_len - 1``; the sampled token is the
+rank-local greedy argmax and ``top_logits`` the first ten logits of the row.
+
+What changes is where the work runs: the model is the fused CUDA path, the
+argmax is a kernel, and the whole step costs one host synchronisation (one
+device-to-host copy of every sampled token and its ten logits, plus the kernel
+status word).
+"""
+
+from __future__ import annotations
+
+import time
+from typing import List, Optional
+
+import numpy as np
+import torch
+
+from pythonintern_b200 import _lib, kernels
+from pythonintern_b200.config import KVCacheConfig, ModelConfig, ShardConfig
+from pythonintern_b200.model.kv_cache import KVCacheManager
+from pythonintern_b200.model.llama import DistributedLLaMAModel
+from pythonintern_b200.model.metadata import PinnedStager, build_metadata
+from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
+from pythonintern_b200.worker.messages import SampledToken, StepResponse
+
+
+class WorkerExecutionEngine:
+    def __init__(self, model_config: ModelConfig, shard_config: ShardConfig, kv_config: KVCacheConfig,
+                 communicator: Optional[DistributedCommunicator] = None, device="cuda"):
+        self.model_config = model_config
+        self.shard_config = shard_config
+        self.kv_config = kv_config
+        self.communicator = communicator
+        dev = torch.device(device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        if kv_config.device in ("cpu", "cuda"):
+            kv_config.device = str(dev)
+        self.kv_manager = KVCacheManager(config=kv_config, model_config=model_config,
+                                         world_size=shard_config.world_size)
+        self.model = DistributedLLaMAModel(config=model_config, rank=shard_config.rank,
+                                           world_size=shard_config.world_size, communicator=communicator, device=dev)
+        self.stager = PinnedStager(dev)
+        self.total_steps_executed = 0
+        self.total_latency_ms = 0.0
+        self.last_h2d_bytes = 0
+        self.last_d2h_bytes = 0
+
+    def _sample(self, logits: torch.Tensor):
+        """Greedy token per row on the device, plus the first ten logits (execution_engine.py:103-108)."""
+        tok = kernels.argmax(logits)
+        return tok, logits[:, :10]
+
+    def execute_step(self, step_request) -> StepResponse:
+        start = time.perf_counter()
+        step_id = step_request.step_id
+        prefill_slots = [s for s in step_request.active_sequences if s.is_prefill]
+        decode_slots = [s for s in step_request.active_sequences if not s.is_prefill]
+        pool = self.kv_manager.pool
+        toks: List[torch.Tensor] = []
+        tops: List[torch.Tensor] = []
+        ids: List[str] = []
+        h2d = 0
+        with torch.no_grad(), torch.cuda.device(self.device):
+            for slot in prefill_slots:
+                prompt = np.asarray([list(slot.prompt_token_ids)], dtype=np.int64)
+                P = prompt.shape[1]
+                table = [list(slot.block_table)]
+                md = build_metadata(np.arange(P, dtype=np.int64)[None, :], table, True, self.device,
+                                    stager=self.stager, extra=prompt)
+                h2d += self.stager.last_bytes
+                logits = self.model(md.extra, None, pool, table, True, step_id, True, metadata=md)
+                t, tl = self._sample(logits)
+                toks.append(t)
+                tops.append(tl)
+                ids.append(slot.seq_id)
+            if decode_slots:
+                tok_ids = np.asarray([[s.current_token_id] for s in decode_slots], dtype=np.int64)
+                pos = np.asarray([[s.current_len - 1] for s in decode_slots], dtype=np.int64)
+                tables = [list(s.block_table) for s in decode_slots]
+                md = build_metadata(pos, tables, False, self.device,
+                                    masked_padding=self.model_config.masked_decode_padding,
+                                    stager=self.stager, extra=tok_ids)
+                h2d += self.stager.last_bytes
+                logits = self.model(md.extra, None, pool, tables, False, step_id, True, metadata=md)
+                t, tl = self._sample(logits)
+                toks.append(t)
+                tops.append(tl)
+                ids.extend(s.seq_id for s in decode_slots)
+            sampled = []
+            if toks:
+                tok_host = torch.cat(toks).cpu().numpy()
+                top_host = torch.cat(tops).cpu().numpy()
+                self.last_d2h_bytes = tok_host.nbytes + top_host.nbytes
+                _lib.check_device_status(self.device, f"step {step_id}")
+                sampled = [SampledToken(seq_id=sid, token_id=int(tok_host[i]),
+                                        top_logits=[float(x) for x in top_host[i]]) for i, sid in enumerate(ids)]
+        self.last_h2d_bytes = h2d
+        elapsed_ms = (time.perf_counter() - start) * 1000.0
+        self.total_steps_executed += 1
+        self.total_latency_ms += elapsed_ms
+        return StepResponse(step_id=step_id, rank=self.shard_config.rank, success=True, sampled_tokens=sampled,
+                            step_latency_ms=elapsed_ms, active_blocks=self.kv_manager.allocated_block_count,
+                            free_blocks=self.kv_manager.free_block_count)
+
+    def evict_sequences(self, seq_ids: List[str]) -> int:
+        return sum(self.kv_manager.free_sequence(sid) for sid in seq_ids)

@@ -1,0 +1,33 @@
+"""The CPU legs of bench.py (the reference-algorithm arm) run without a GPU."""
+
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def test_cpu_sample_small_shape():
+    import bench
+    from pythonintern_b200 import workloads
+    cfg = workloads.tinyllama_config(num_layers=2)
+    cfg.vocab_size = 1024
+    t = bench.cpu_sample(cfg, batch=2, ctx=64, seed=0)
+    assert 0 < t < 60
+
+
+def test_reference_arm_prints_one_json_line():
+    env = dict(os.environ, RANK="0")
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "0", "--cpu-sample-batch", "1", "--ctx", "64"],
+                         capture_output=True, text=True, timeout=600, env=env)
+    assert out.returncode == 0, out.stderr
+    lines = [l for l in out.stdout.splitlines() if l.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["value"] > 0 and d["cpu_baseline"]["kind"] == "port"
+    assert d["e2e"]["h2d_bytes_per_step"] == 0

@@ -1,0 +1,271 @@
+"""Module- and model-level parity on the GPU.
+
+* The reference's own unit tests (tests/test_tensor_parallel.py, tests/test_kv_cache.py)
+  re-run against this package's modules.
+* The golden vectors from the reference (tests/golden/units.npz): attention prefill +
+  unmasked decode, SwiGLU MLP, transformer block, paged pool roundtrip; float32 at 1e-5.
+* The Tiny LLaMA workload end to end through WorkerExecutionEngine.execute_step:
+  32 greedy tokens identical to the reference, per-layer activations within 1e-5.
+* bf16 layers of the TinyLlama and Llama-3-8B shapes against the oracle at 2e-2.
+"""
+
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from pythonintern_b200 import _lib, workloads  # noqa: E402
+from pythonintern_b200.config import KVCacheConfig, ModelConfig, ShardConfig  # noqa: E402
+from pythonintern_b200.model.attention import DistributedAttention  # noqa: E402
+from pythonintern_b200.model.kv_cache import BlockTable, KVCacheManager, PhysicalKVCachePool  # noqa: E402
+from pythonintern_b200.model.llama import DistributedLLaMAModel, DistributedTransformerBlock  # noqa: E402
+from pythonintern_b200.model.mlp import DistributedMLP  # noqa: E402
+from pythonintern_b200.tensor_parallel.layers import ColumnParallelLinear, RMSNorm, RowParallelLinear  # noqa: E402
+from pythonintern_b200.worker.execution_engine import WorkerExecutionEngine  # noqa: E402
+from pythonintern_b200.worker.messages import SequenceSlot, StepRequest  # noqa: E402
+
+DEV = torch.device("cuda", 0)
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def rel(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def units():
+    return np.load(os.path.join(GOLD, "units.npz"))
+
+
+# ------------------------------------------------------------------ reference unit tests, re-targeted
+def test_column_parallel_linear():
+    """tests/test_tensor_parallel.py:28-58 on this package's ColumnParallelLinear."""
+    torch.manual_seed(0)
+    full = nn.Linear(32, 64, bias=False)
+    x = torch.randn(2, 4, 32)
+    expected = full(x)
+    r0 = ColumnParallelLinear(32, 64, bias=False, rank=0, world_size=2, device=DEV)
+    r1 = ColumnParallelLinear(32, 64, bias=False, rank=1, world_size=2, device=DEV)
+    with torch.no_grad():
+        r0.weight.copy_(full.weight.t()[:, 0:32])
+        r1.weight.copy_(full.weight.t()[:, 32:64])
+    out = torch.cat([r0(x.to(DEV)), r1(x.to(DEV))], dim=-1).cpu()
+    assert torch.allclose(expected, out, atol=1e-5)
+    assert r0.weight.shape == (32, 32) and r0.state_dict()["weight"].shape == (32, 32)
+
+
+def test_row_parallel_linear_single_rank():
+    torch.manual_seed(1)
+    full = nn.Linear(32, 16, bias=False)
+    x = torch.randn(2, 4, 32)
+    row = RowParallelLinear(32, 16, bias=False, rank=0, world_size=1, device=DEV)
+    with torch.no_grad():
+        row.weight.copy_(full.weight.t())
+    assert torch.allclose(full(x), row(x.to(DEV), step_tag="t").cpu(), atol=1e-5)
+
+
+def test_rmsnorm_module():
+    """tests/test_tensor_parallel.py:121-131."""
+    norm = RMSNorm(64, eps=1e-5, device=DEV)
+    y = norm(torch.randn(2, 5, 64, device=DEV))
+    var = y.pow(2).mean(dim=-1)
+    assert y.shape == (2, 5, 64)
+    assert torch.allclose(var, torch.ones_like(var), atol=1e-3)
+
+
+def test_pool_roundtrip_golden(units):
+    """tests/test_kv_cache.py:26-56 plus the permuted-table golden."""
+    pool = PhysicalKVCachePool(12, 16, 2, 32, 2, device=DEV)
+    table = [int(b) for b in units["pool_table"]]
+    kin, vin = torch.from_numpy(units["pool_k_in"]), torch.from_numpy(units["pool_v_in"])
+    for t in range(50):
+        pool.store_kv(1, table[t // 16], t % 16, kin[t].to(DEV), vin[t].to(DEV))
+    k, v = pool.read_kv_sequence(1, table, 41)
+    assert np.array_equal(k.cpu().numpy(), units["pool_k_out"]) and np.array_equal(v.cpu().numpy(), units["pool_v_out"])
+    assert np.array_equal(pool.k_cache.cpu().numpy(), units["pool_k_cache"])
+
+
+def test_kv_manager_lifecycle():
+    """tests/test_kv_cache.py:59-83."""
+    mgr = KVCacheManager(KVCacheConfig(block_size=16, num_blocks=10, device=str(DEV)),
+                         ModelConfig(hidden_dim=64, num_heads=4, num_kv_heads=2, num_layers=2), world_size=1)
+    assert mgr.free_block_count == 10
+    table = mgr.allocate_blocks_for_sequence("req_1", num_tokens=30)
+    assert len(table.physical_block_ids) == 2 and mgr.free_block_count == 8
+    mgr.append_token("req_1")
+    mgr.append_token("req_1")
+    assert len(table.physical_block_ids) == 2
+    mgr.append_token("req_1")
+    assert len(table.physical_block_ids) == 3 and mgr.free_block_count == 7
+    assert mgr.free_sequence("req_1") == 3 and mgr.free_block_count == 10
+
+
+# ------------------------------------------------------------------ reference golden vectors
+def _small_cfg():
+    return ModelConfig(vocab_size=64, hidden_dim=128, num_layers=1, num_heads=4, num_kv_heads=2,
+                       intermediate_dim=96, max_seq_len=256)
+
+
+def test_attention_golden_prefill_and_unmasked_decode(units):
+    attn = DistributedAttention(_small_cfg(), layer_idx=0, device=DEV)
+    with torch.no_grad():
+        for n in ("q_proj", "k_proj", "v_proj", "out_proj"):
+            getattr(attn, n).weight.copy_(torch.from_numpy(units[f"attn_{n}"]))
+    pool = PhysicalKVCachePool(16, 16, 2, 32, 1, device=DEV)
+    tables = [[int(b) for b in t] for t in units["attn_tables"]]
+    lens = [int(x) for x in units["attn_lens"]]
+    for b in range(2):
+        x = torch.from_numpy(units[f"attn_prefill{b}_x"]).to(DEV)
+        y = attn(x, torch.arange(lens[b])[None], pool, [tables[b]], True, 0)
+        assert rel(y.cpu().numpy(), units[f"attn_prefill{b}_y"]) < 1e-5
+    y = attn(torch.from_numpy(units["attn_decode_x"]).to(DEV), torch.from_numpy(units["attn_decode_pos"]),
+             pool, tables, False, 1)
+    torch.cuda.synchronize()
+    _lib.check_device_status(DEV, "attention golden")
+    assert rel(y.cpu().numpy(), units["attn_decode_y"]) < 1e-5
+    np.testing.assert_allclose(pool.k_cache.cpu().numpy(), units["attn_k_cache"], atol=1e-5)
+    np.testing.assert_allclose(pool.v_cache.cpu().numpy(), units["attn_v_cache"], atol=1e-5)
+
+
+def test_mlp_golden(units):
+    mlp = DistributedMLP(_small_cfg(), layer_idx=0, device=DEV)
+    with torch.no_grad():
+        for n in ("gate_proj", "up_proj", "down_proj"):
+            getattr(mlp, n).weight.copy_(torch.from_numpy(units[f"mlp_{n}"]))
+    y = mlp(torch.from_numpy(units["mlp_x"]).to(DEV))
+    assert rel(y.cpu().numpy(), units["mlp_y"]) < 1e-5
+
+
+def test_block_golden(units):
+    blk = DistributedTransformerBlock(_small_cfg(), layer_idx=0, device=DEV)
+    sd = {k[len("blk."):]: torch.from_numpy(units[k]) for k in units.files if k.startswith("blk.")}
+    blk.load_state_dict(sd)
+    pool = PhysicalKVCachePool(4, 16, 2, 32, 1, device=DEV)
+    yp = blk(torch.from_numpy(units["blk_xp"]).to(DEV), torch.arange(5)[None], pool, [[3]], True, 0)
+    assert rel(yp.cpu().numpy(), units["blk_yp"]) < 1e-5
+    yd = blk(torch.from_numpy(units["blk_xd"]).to(DEV), torch.tensor([[5]]), pool, [[3]], False, 1)
+    assert rel(yd.cpu().numpy(), units["blk_yd"]) < 1e-5
+
+
+# ------------------------------------------------------------------ Tiny LLaMA end to end
+def _tiny_engine(num_blocks=64):
+    cfg = workloads.tiny_config()
+    eng = WorkerExecutionEngine(cfg, ShardConfig(0, 1), KVCacheConfig(16, num_blocks, str(DEV)), None, DEV)
+    eng.model.load_state_dict(workloads.reference_init_state_dict(cfg, 0))
+    return eng
+
+
+def test_tiny_workload_tokens_identical_to_reference():
+    """Config 1: 8 prompts, 32 greedy tokens through execute_step; tokens == the reference's."""
+    gold = np.load(os.path.join(GOLD, "tiny_e2e_tp1.npz"))
+    eng = _tiny_engine()
+    prompts = workloads.tiny_prompts()
+    ids = [f"req_{i}" for i in range(8)]
+    for sid, p in zip(ids, prompts):
+        eng.kv_manager.allocate_blocks_for_sequence(sid, len(p))
+    lens = {sid: len(p) for sid, p in zip(ids, prompts)}
+    cur = {}
+    all_toks, all_tops = [], []
+    for step in range(32):
+        if step == 0:
+            slots = [SequenceSlot(sid, True, p, 0, len(p), list(eng.kv_manager.block_tables[sid].physical_block_ids))
+                     for sid, p in zip(ids, prompts)]
+        else:
+            slots = []
+            for sid in ids:
+                eng.kv_manager.append_token(sid)
+                lens[sid] += 1
+                slots.append(SequenceSlot(sid, False, [], cur[sid], lens[sid],
+                                          list(eng.kv_manager.block_tables[sid].physical_block_ids)))
+        resp = eng.execute_step(StepRequest(step, slots))
+        assert resp.success and [t.seq_id for t in resp.sampled_tokens] == ids
+        toks = [t.token_id for t in resp.sampled_tokens]
+        cur = dict(zip(ids, toks))
+        all_toks.append(toks)
+        all_tops.append([t.top_logits for t in resp.sampled_tokens])
+    assert np.array_equal(np.asarray(all_toks), gold["tokens"])
+    np.testing.assert_allclose(np.asarray(all_tops), gold["top_logits"], atol=1e-4, rtol=1e-5)
+    for i, sid in enumerate(ids):
+        t = [int(b) for b in gold["block_tables"][i] if b >= 0]
+        assert eng.kv_manager.block_tables[sid].physical_block_ids == t
+
+
+def test_tiny_per_layer_activations():
+    gold = np.load(os.path.join(GOLD, "tiny_e2e_tp1.npz"))
+    eng = _tiny_engine()
+    prompts = workloads.tiny_prompts()
+    table = eng.kv_manager.allocate_blocks_for_sequence("req_0", len(prompts[0])).physical_block_ids
+    trace = []
+    P = len(prompts[0])
+    eng.model(torch.tensor([prompts[0]], device=DEV), torch.arange(P)[None], eng.kv_manager.pool, [table], True,
+              0, trace=trace)
+    for layer in range(4):
+        assert rel(trace[layer].cpu().numpy(), gold["prefill_trace"][layer]) < 1e-5
+
+
+# ------------------------------------------------------------------ bf16 layers vs the oracle
+def _bf16_layer_check(cfg, prompts_len, n_decode, seed, tol=2e-2):
+    sd = workloads.synthetic_state_dict(cfg, seed=seed)
+    model = DistributedLLaMAModel(cfg, device=DEV)
+    model.load_state_dict(sd)
+    nb = 64
+    pool = PhysicalKVCachePool(nb, 16, cfg.num_kv_heads, cfg.head_dim, cfg.num_layers, DEV, "bfloat16")
+    ocfg = oracle.OracleConfig(cfg.vocab_size, cfg.hidden_dim, cfg.num_layers, cfg.num_heads, cfg.num_kv_heads,
+                               cfg.intermediate_dim, cfg.max_seq_len, cfg.rms_norm_eps)
+    om = oracle.OracleModel(ocfg, [{k: v.float().numpy() for k, v in sd.items()}],
+                            [oracle.KVPool(cfg.num_layers, nb, 16, cfg.num_kv_heads, cfg.head_dim)])
+    gen = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(nb, generator=gen).tolist()
+    tables, k = [], 0
+    for P in prompts_len:
+        n = math.ceil((P + n_decode) / 16)
+        tables.append(perm[k:k + n])
+        k += n
+    worst = 0.0
+    last = []
+    for b, P in enumerate(prompts_len):
+        toks = torch.randint(0, cfg.vocab_size, (1, P), generator=gen)
+        tr, otr = [], []
+        lg = model(toks.to(DEV), torch.arange(P)[None], pool, [tables[b]], True, 0, trace=tr)
+        olg = om.forward(toks.numpy(), np.arange(P)[None], [tables[b]], True, trace=otr)
+        for a, o in zip(tr, otr):
+            worst = max(worst, rel(a.cpu().numpy(), o[0]))
+        last.append(int(torch.argmax(lg[0])))
+    lens = list(prompts_len)
+    for step in range(n_decode):
+        toks = torch.tensor([[t] for t in last])
+        pos = torch.tensor([[n] for n in lens])
+        tr, otr = [], []
+        lg = model(toks.to(DEV), pos, pool, tables, False, step + 1, trace=tr)
+        olg = om.forward(toks.numpy(), pos.numpy(), tables, False, trace=otr)
+        for a, o in zip(tr, otr):
+            worst = max(worst, rel(a.cpu().numpy(), o[:, 0]))
+        last = [int(x) for x in torch.argmax(lg, dim=-1).cpu()]
+        lens = [n + 1 for n in lens]
+    torch.cuda.synchronize()
+    _lib.check_device_status(DEV, "bf16 model")
+    assert worst < tol, f"worst per-layer relative error {worst:.3e}"
+    return worst
+
+
+def test_tinyllama_shape_bf16_layers():
+    cfg = workloads.tinyllama_config(num_layers=2)
+    cfg.vocab_size = 4096  # the layer shapes are the point; a small vocab keeps the oracle fast
+    _bf16_layer_check(cfg, [37, 130, 64], 3, seed=11)
+
+
+def test_llama3_8b_shape_bf16_layer():
+    cfg = workloads.llama3_8b_config(num_layers=1, max_seq_len=512)
+    cfg.vocab_size = 4096
+    _bf16_layer_check(cfg, [150, 17], 2, seed=12)
