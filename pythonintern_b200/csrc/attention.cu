@@ -300,11 +300,15 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 struct AttnWs {
   size_t counters, ml, o, total;
 };
+// The counter region has a FIXED size so that calls with different row counts never
+// read each other's partial states as counters.
+constexpr size_t kAttnCounterSlots = 16384;
+
 static AttnWs attn_ws_layout(int n_rows, int nq, int nkv, int hd, int splits) {
   AttnWs w{};
   if (splits <= 1) return w;
   w.counters = 0;
-  w.ml = align256((size_t)n_rows * nkv * sizeof(int));
+  w.ml = kAttnCounterSlots * sizeof(int);
   w.o = w.ml + align256((size_t)n_rows * nq * splits * 2 * sizeof(float));
   w.total = w.o + align256((size_t)n_rows * nq * splits * hd * sizeof(float));
   return w;
@@ -364,6 +368,9 @@ int b2_paged_attention(const void* q, int64_t ld_q, int n_rows, int nq, int nkv,
   b2::AttnWs lay = b2::attn_ws_layout(n_rows, nq, nkv, head_dim, num_splits);
   b2::AttnParams p{};
   if (num_splits > 1) {
+    B2_CHECK_ARG((size_t)n_rows * nkv <= b2::kAttnCounterSlots,
+                 "b2_paged_attention: n_rows * nkv = %d exceeds %zu with num_splits > 1", n_rows * nkv,
+                 b2::kAttnCounterSlots);
     B2_CHECK_ARG(workspace && workspace_bytes >= lay.total,
                  "b2_paged_attention: workspace of %zu bytes needed, %zu given", lay.total, workspace_bytes);
     char* ws = static_cast<char*>(workspace);

@@ -356,28 +356,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       __threadfence();
       const int64_t split_stride = (int64_t)p.n_tiles * p.m_tiles * tile_elems;
       const float* base = p.ws + slot * tile_elems;
+      const int ncols = min(BN, M - m0);
+      const int nsplit = p.splits;
       if (p.epi == kEpiStore) {
-        const int n = local_tile * BM + r;
-        if (n < seg_n) {
-          const int64_t col = (int64_t)seg_col + n;
-          const float bv = p.bias ? p.bias[col] : 0.f;
-          for (int c = 0; c < BN && m0 + c < M; ++c) {
-            float acc = 0.f;
-            for (int s = 0; s < p.splits; ++s) acc += __ldcg(base + s * split_stride + (int64_t)c * BM + r);
-            st_dyn(p.y, p.y_dtype, (int64_t)(m0 + c) * p.ldy + col, acc + bv);
+        // Each warp reduces whole token columns (128 contiguous floats = 32 lanes x float4),
+        // 4 columns per pass with every split's loads issued before any store.
+        const int r4 = lane * 4;
+        const int n0 = local_tile * BM + r4;
+        float bv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) bv[e] = (p.bias && n0 + e < seg_n) ? p.bias[seg_col + n0 + e] : 0.f;
+        for (int cb = warp * 4; cb < ncols; cb += 16) {
+          float4 acc[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int sp = 0; sp < nsplit; ++sp) {
+            const float* src = base + sp * split_stride + r4;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              if (cb + u < ncols) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(src + (int64_t)(cb + u) * BM));
+                acc[u].x += v.x; acc[u].y += v.y; acc[u].z += v.z; acc[u].w += v.w;
+              }
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (cb + u >= ncols) continue;
+            const int64_t rowoff = (int64_t)(m0 + cb + u) * p.ldy + seg_col;
+            const float vals[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (n0 + e < seg_n) st_dyn(p.y, p.y_dtype, rowoff + n0 + e, vals[e] + bv[e]);
           }
         }
-      } else if (r < 64) {
-        const int n = local_tile * 64 + r;
-        if (n < p.seg_n[0]) {
-          for (int c = 0; c < BN && m0 + c < M; ++c) {
-            float g = 0.f, u = 0.f;
-            for (int s = 0; s < p.splits; ++s) {
-              g += __ldcg(base + s * split_stride + (int64_t)c * BM + r);
-              u += __ldcg(base + s * split_stride + (int64_t)c * BM + r + 64);
-            }
-            st_dyn(p.y, p.y_dtype, (int64_t)(m0 + c) * p.ldy + n, silu_f32(g) * u);
+      } else {
+        // SwiGLU: lanes 0-15 / 16-31 take two token columns; each lane holds 4 gate rows
+        // (TMEM lanes 0-63 of the tile) and the matching 4 up rows (64-127).
+        const int half = lane >> 4;
+        const int r4 = (lane & 15) * 4;
+        const int n0 = local_tile * 64 + r4;
+        for (int cb = warp * 2 + half; cb < ncols; cb += 8) {
+          float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), us = gs;
+          for (int sp = 0; sp < nsplit; ++sp) {
+            const float* src = base + sp * split_stride + (int64_t)cb * BM + r4;
+            const float4 gv = __ldcg(reinterpret_cast<const float4*>(src));
+            const float4 uv = __ldcg(reinterpret_cast<const float4*>(src + 64));
+            gs.x += gv.x; gs.y += gv.y; gs.z += gv.z; gs.w += gv.w;
+            us.x += uv.x; us.y += uv.y; us.z += uv.z; us.w += uv.w;
           }
+          const int64_t rowoff = (int64_t)(m0 + cb) * p.ldy;
+          const float g4[4] = {gs.x, gs.y, gs.z, gs.w}, u4[4] = {us.x, us.y, us.z, us.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (n0 + e < seg_n) st_dyn(p.y, p.y_dtype, rowoff + n0 + e, silu_f32(g4[e]) * u4[e]);
         }
       }
     }
@@ -462,10 +494,15 @@ static Plan make_plan(int M, int n_tiles, int K) {
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Workspace layout: a FIXED-size counter region (so that launches of different tile
+// counts never see each other's partial tiles as counters), then the partial tiles.
+constexpr size_t kCounterSlots = 65536;
+constexpr size_t kCounterBytes = kCounterSlots * sizeof(int);
+
 static size_t plan_ws_bytes(const Plan& pl) {
   if (pl.splits <= 1) return 0;
   const size_t units = (size_t)pl.n_tiles * pl.m_tiles;
-  return align256(units * sizeof(int)) + (size_t)pl.splits * units * BM * pl.BN * sizeof(float);
+  return kCounterBytes + (size_t)pl.splits * units * BM * pl.BN * sizeof(float);
 }
 
 template <int BN>
@@ -548,9 +585,9 @@ int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int n
   p.ldy = ldy;
   p.y_dtype = y_dtype;
   if (need > 0) {
-    const size_t units = (size_t)pl.n_tiles * pl.m_tiles;
+    B2_CHECK_ARG((size_t)pl.n_tiles * pl.m_tiles <= tc::kCounterSlots, "gemm_tc: too many tiles for split-K");
     p.counters = reinterpret_cast<int*>(ws);
-    p.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + tc::align256(units * sizeof(int)));
+    p.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + tc::kCounterBytes);
   }
   p.status = status;
 
