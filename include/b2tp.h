@@ -137,6 +137,25 @@ int b2_paged_attention(const void* q, int64_t ld_q, int n_rows, int nq, int nkv,
                        float scale, void* out, int64_t ld_out, int dtype, void* workspace,
                        size_t workspace_bytes, int num_splits, int32_t* status, b2_stream_t stream);
 
+/* Allocation-free variant of b2_paged_attention (no counterpart in the reference).
+ * For callers that cannot allocate device memory: a host that reaches this library
+ * only through the plain C ABI (cgo, JNI, ctypes) and has no device allocator of its
+ * own, or a worker whose device memory was handed in full to another runtime's pool
+ * at start-up, where a cudaMalloc would fail or fragment that pool.  The split
+ * scratch lives in a 4 MiB static array inside the library (every GPU that loads the
+ * library holds it until the process exits); calls needing more are rejected with
+ * B2_EINVAL.  The first call on a device looks up the array's device address with
+ * cudaGetSymbolAddress; make that first call before any stream capture.  All calls
+ * share the array, so calls that overlap on the GPU (different streams without
+ * ordering) race; order them on one stream.  Allocates nothing: no cudaMalloc or
+ * cudaFree.  Arguments and result are those of b2_paged_attention. */
+int b2_paged_attention_noalloc(const void* q, int64_t ld_q, int n_rows, int nq, int nkv, int head_dim,
+                               const void* k_cache, const void* v_cache, int layer, int num_blocks,
+                               int block_size, const int32_t* block_tables, int table_stride,
+                               const int32_t* table_index, const int32_t* ctx_lens, int compat_pad,
+                               float scale, void* out, int64_t ld_out, int dtype, int num_splits,
+                               int32_t* status, b2_stream_t stream);
+
 /* ---------------------------------------------------------------- greedy sampling
  * out[r] = first index of the maximum of logits[r, 0:cols]   (execution_engine.py:103,133) */
 int b2_argmax(const float* logits, int64_t ld, int rows, int cols, int64_t* out, b2_stream_t stream);

@@ -51,6 +51,10 @@ _SIGS = {
                                     _c_int, _c_int, _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_int,
                                     _c_float, _c_void_p, _c_i64, _c_int, _c_void_p, _c_size, _c_int,
                                     _c_void_p, _c_void_p]),
+    "b2_paged_attention_noalloc": (_c_int, [_c_void_p, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_void_p,
+                                            _c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_int, _c_void_p,
+                                            _c_void_p, _c_int, _c_float, _c_void_p, _c_i64, _c_int, _c_int,
+                                            _c_void_p, _c_void_p]),
     "b2_argmax": (_c_int, [_c_void_p, _c_i64, _c_int, _c_int, _c_void_p, _c_void_p]),
     "b2_comm_handle_bytes": (_c_size, []),
     "b2_comm_create": (_c_int, [_c_int, _c_int, _c_size, ctypes.POINTER(_c_void_p)]),

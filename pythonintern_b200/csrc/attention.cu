@@ -16,6 +16,8 @@
 //    last CTA of the row to finish, found with an atomic counter).
 //  * compat_pad reproduces the reference's unmasked zero padding
 //    (attention.py:190-203): (max_ctx - ctx) extra keys with score 0 and value 0.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace b2 {
@@ -337,6 +339,32 @@ static int launch_hd(int hd, int rep, const AttnParams& p, dim3 grid, cudaStream
   }
 }
 
+// Scratch of b2_paged_attention_noalloc: a fixed array in the library's own device
+// memory, present on every GPU that loads the library until the process exits.
+constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+constexpr int kNoAllocMaxDevices = 64;
+static void* g_noalloc_scratch_addr[kNoAllocMaxDevices] = {nullptr};
+static std::mutex g_noalloc_mutex;
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device.
+// The name itself is only a host-side stand-in and must never reach a kernel.
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  B2_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(B2_ENOTSUP, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_scratch_addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(B2_ECUDA, "cudaGetSymbolAddress(scratch) on device %d: %s", dev, cudaGetErrorString(e));
+    g_noalloc_scratch_addr[dev] = p;
+  }
+  *out = g_noalloc_scratch_addr[dev];
+  return B2_OK;
+}
+
 }  // namespace b2
 
 extern "C" {
@@ -402,6 +430,33 @@ int b2_paged_attention(const void* q, int64_t ld_q, int n_rows, int nq, int nkv,
   const int rep = nq / nkv;
   if (dtype == B2_BF16) return b2::launch_hd<__nv_bfloat16>(head_dim, rep, p, grid, stream);
   return b2::launch_hd<float>(head_dim, rep, p, grid, stream);
+}
+
+// Same computation as b2_paged_attention, with the split scratch taken from the
+// library's static device array instead of a caller-provided workspace.
+int b2_paged_attention_noalloc(const void* q, int64_t ld_q, int n_rows, int nq, int nkv, int head_dim,
+                               const void* k_cache, const void* v_cache, int layer, int num_blocks,
+                               int block_size, const int32_t* block_tables, int table_stride,
+                               const int32_t* table_index, const int32_t* ctx_lens, int compat_pad,
+                               float scale, void* out, int64_t ld_out, int dtype, int num_splits,
+                               int32_t* status, b2_stream_t stream) {
+  void* scratch = nullptr;
+  if (num_splits > 1) {
+    B2_CHECK_ARG(n_rows >= 0 && nq > 0 && nkv > 0 && head_dim > 0 && num_splits <= 1024,
+                 "b2_paged_attention_noalloc: bad sizes");
+    const size_t need = b2_paged_attention_workspace_bytes(n_rows, nq, nkv, head_dim, num_splits);
+    B2_CHECK_ARG(need <= b2::kNoAllocScratchBytes,
+                 "b2_paged_attention_noalloc: this call needs %zu bytes of split scratch but the static "
+                 "array holds %zu; use fewer splits or rows, or b2_paged_attention with a workspace",
+                 need, b2::kNoAllocScratchBytes);
+    const int rc = b2::noalloc_scratch(&scratch);
+    if (rc) return rc;
+    // The array keeps the previous call's contents: zero the split counters this call uses.
+    if (n_rows > 0) B2_TRY_CUDA(cudaMemsetAsync(scratch, 0, (size_t)n_rows * nkv * sizeof(int), stream));
+  }
+  return b2_paged_attention(q, ld_q, n_rows, nq, nkv, head_dim, k_cache, v_cache, layer, num_blocks, block_size,
+                            block_tables, table_stride, table_index, ctx_lens, compat_pad, scale, out, ld_out,
+                            dtype, scratch, scratch ? b2::kNoAllocScratchBytes : 0, num_splits, status, stream);
 }
 
 }  // extern "C"
