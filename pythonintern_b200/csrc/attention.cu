@@ -51,6 +51,118 @@ __device__ __forceinline__ float safe_exp2_diff(float a, float m) {
   return a == -INFINITY ? 0.f : exp2f(a - m);
 }
 
+// Merges the per-warp softmax states (sm_m/sm_l [nw][REP], sm_acc [nw][REP][HD]) of one
+// (row, kv head, split), then either stores the output (one split) or publishes the
+// split's state and lets the last split of (row, kv head) merge all of them.  Compat
+// padding adds (max_ctx - ctx) keys of score 0 and value 0 to the final denominator.
+template <typename T, int HD, int REP>
+__device__ void attn_finalize(const AttnParams& p, const float* sm_m, const float* sm_l, const float* sm_acc,
+                              int nw, int row, int g, int split, int ctx) {
+  __shared__ float red[32];
+  __shared__ int sm_flag;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps_block = blockDim.x >> 5;
+  // Compat padding needs the longest context of the call.
+  int max_ctx = ctx;
+  if (p.compat_pad) {
+    float mx = 0.f;
+    for (int i = threadIdx.x; i < p.n_rows; i += blockDim.x) mx = fmaxf(mx, (float)p.ctx_lens[i]);
+    mx = warp_max(mx);
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    float all = red[0];
+#pragma unroll
+    for (int w = 1; w < nwarps_block; ++w) all = fmaxf(all, red[w]);
+    max_ctx = (int)all;
+  }
+  const int npad = p.compat_pad ? max(0, max_ctx - ctx) : 0;
+
+  T* outp = reinterpret_cast<T*>(p.out) + (int64_t)row * p.ld_out + (int64_t)g * REP * HD;
+  const int64_t head0 = (int64_t)row * p.nq + g * REP;
+
+  if (p.splits == 1) {
+    for (int i = threadIdx.x; i < REP * HD; i += blockDim.x) {
+      const int r = i / HD, d = i % HD;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < nw; ++w) M = fmaxf(M, sm_m[w * REP + r]);
+      float L = 0.f, A = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int w = 0; w < nw; ++w) {
+          const float f = safe_exp2_diff(sm_m[w * REP + r], M);
+          L += sm_l[w * REP + r] * f;
+          A += sm_acc[(w * REP + r) * HD + d] * f;
+        }
+      }
+      if (npad > 0) {
+        const float Mp = fmaxf(M, 0.f);
+        const float f = M == -INFINITY ? 0.f : exp2f(M - Mp);
+        L = L * f + (float)npad * exp2f(-Mp);
+        A = A * f;
+      }
+      outp[i] = from_f32<T>(L > 0.f ? A / L : 0.f);
+    }
+    return;
+  }
+
+  // Write this split's partial state, then let the last split of (row, g) merge.
+  for (int i = threadIdx.x; i < REP * HD; i += blockDim.x) {
+    const int r = i / HD, d = i % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < nw; ++w) M = fmaxf(M, sm_m[w * REP + r]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < nw; ++w) {
+        const float f = safe_exp2_diff(sm_m[w * REP + r], M);
+        L += sm_l[w * REP + r] * f;
+        A += sm_acc[(w * REP + r) * HD + d] * f;
+      }
+    }
+    const int64_t h = head0 + r;
+    p.ws_o[(h * p.splits + split) * HD + d] = A;
+    if (d == 0) {
+      p.ws_ml[(h * p.splits + split) * 2 + 0] = M;
+      p.ws_ml[(h * p.splits + split) * 2 + 1] = L;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* ctr = p.counters + (int64_t)row * p.nkv + g;
+    const int prev = atomicAdd(ctr, 1);
+    const int last = prev == p.splits - 1;
+    if (last) *ctr = 0;  // ready for the next launch
+    sm_flag = last;
+  }
+  __syncthreads();
+  if (!sm_flag) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < REP * HD; i += blockDim.x) {
+    const int r = i / HD, d = i % HD;
+    const int64_t h = head0 + r;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, __ldcg(&p.ws_ml[(h * p.splits + s2) * 2]));
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+      for (int s2 = 0; s2 < p.splits; ++s2) {
+        const float f = safe_exp2_diff(__ldcg(&p.ws_ml[(h * p.splits + s2) * 2]), M);
+        L += __ldcg(&p.ws_ml[(h * p.splits + s2) * 2 + 1]) * f;
+        A += __ldcg(&p.ws_o[(h * p.splits + s2) * HD + d]) * f;
+      }
+    }
+    if (npad > 0) {
+      const float Mp = fmaxf(M, 0.f);
+      const float f = M == -INFINITY ? 0.f : exp2f(M - Mp);
+      L = L * f + (float)npad * exp2f(-Mp);
+      A = A * f;
+    }
+    outp[i] = from_f32<T>(L > 0.f ? A / L : 0.f);
+  }
+}
+
 template <typename T, int HD, int REP>
 __global__ void __launch_bounds__(kAttnWarps * 32) paged_attn_simt_kernel(AttnParams p) {
   constexpr int VEC = 16 / sizeof(T);
@@ -61,8 +173,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_attn_simt_kernel(AttnPa
 
   __shared__ float sm_m[kAttnWarps][REP], sm_l[kAttnWarps][REP];
   __shared__ float sm_acc[kAttnWarps][REP][HD];
-  __shared__ int sm_flag;
-  __shared__ float red[32];
 
   const int split = blockIdx.x, g = blockIdx.y, row = blockIdx.z;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -196,104 +306,256 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_attn_simt_kernel(AttnPa
   }
   __syncthreads();
 
-  // Compat padding needs the longest context of the call.
-  int max_ctx = ctx;
-  if (p.compat_pad) {
-    float mx = 0.f;
-    for (int i = threadIdx.x; i < p.n_rows; i += blockDim.x) mx = fmaxf(mx, (float)p.ctx_lens[i]);
-    mx = warp_max(mx);
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
-    float all = red[0];
-#pragma unroll
-    for (int w = 1; w < kAttnWarps; ++w) all = fmaxf(all, red[w]);
-    max_ctx = (int)all;
-  }
-  const int npad = p.compat_pad ? max(0, max_ctx - ctx) : 0;
+  attn_finalize<T, HD, REP>(p, &sm_m[0][0], &sm_l[0][0], &sm_acc[0][0][0], kAttnWarps, row, g, split, ctx);
+}
 
-  T* outp = reinterpret_cast<T*>(p.out) + (int64_t)row * p.ld_out + (int64_t)g * REP * HD;
-  const int64_t head0 = (int64_t)row * p.nq + g * REP;
+// ---------------------------------------------------------------------------------------
+// bf16 path: tensor-core (mma.sync m16n8k16) decode attention with cp.async pipelines.
+//
+// A CTA owns one (row, kv head, split); each of its 4 warps walks every 4th KV block
+// of the CTA's run with its own STAGES-deep cp.async ring of whole blocks (16 token
+// rows of K and of V for this kv head), so 12 blocks per CTA are in flight.  Rows are
+// stored in shared memory with their 16-byte chunks XOR-swizzled by (row & 7), which
+// keeps the ldmatrix reads below free of bank conflicts.  Per block a warp computes
+//   S[16 x 16]  = Q[16 x HD] . K^T   (the REP <= 8 query heads of the group are rows
+//                                     0..REP-1 of the 16-row MMA tile, 8 k-steps)
+//   O[16 x HD] += P[16 x 16] . V      (P reused from the S accumulator registers)
+// with an online softmax in the log2 domain.  The float32 softmax statistics, the
+// per-warp merge and the split merge are shared with the SIMT kernel.
+constexpr int kMmaWarps = 4;
+constexpr int kMmaStages = 3;
 
-  if (p.splits == 1) {
-    for (int i = threadIdx.x; i < REP * HD; i += blockDim.x) {
-      const int r = i / HD, d = i % HD;
-      float M = -INFINITY;
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr) : "memory");
+}
+// D = A . B + D, m16n8k16, bf16 inputs, f32 accumulators.
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int HD>
+struct MmaCfg {
+  static constexpr int ROWB = HD * 2;         // bytes of one token row of one kv head
+  static constexpr int CHUNKS = ROWB / 16;    // 16-byte chunks per row
+  static constexpr int SWZ = CHUNKS < 8 ? CHUNKS - 1 : 7;
+  static constexpr int BLKB = 16 * ROWB;      // one K (or V) block
+  static constexpr int STAGEB = 2 * BLKB;     // K + V
+  static constexpr size_t SMEM = (size_t)kMmaWarps * kMmaStages * STAGEB;
+};
+
+template <int HD>
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return (uint32_t)(row * MmaCfg<HD>::ROWB + ((chunk ^ (row & MmaCfg<HD>::SWZ)) << 4));
+}
+
+template <int HD, int REP>
+__global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnParams p) {
+  using C = MmaCfg<HD>;
+  static_assert(REP <= 8, "the MMA tile holds up to 8 query heads per kv head");
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int split = blockIdx.x, g = blockIdx.y, row = blockIdx.z;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int qr = lane >> 2, qt = lane & 3;  // MMA fragment row / column-pair of this lane
+  const int ctx = max(0, p.ctx_lens[row]);
+  const int bs = 16;
+  const int nblk = (ctx + bs - 1) / bs;
+  const int bps = (nblk + p.splits - 1) / p.splits;
+  const int blk0 = min(nblk, split * bps);
+  const int blk1 = min(nblk, blk0 + bps);
+  const int trow = p.table_index ? p.table_index[row] : row;
+  const int32_t* table = p.tables + (int64_t)trow * p.table_stride;
+  const int n_w = blk1 - blk0 > warp ? (blk1 - blk0 - warp + kMmaWarps - 1) / kMmaWarps : 0;
+
+  // Q fragments (A operand rows 0..7 = the REP heads, rows 8..15 = zero padding).
+  uint32_t qa[HD / 16][2];
+  {
+    const __nv_bfloat16* qrow_ptr =
+        reinterpret_cast<const __nv_bfloat16*>(p.q) + (int64_t)row * p.ld_q + (int64_t)(g * REP + qr) * HD;
 #pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w][r]);
-      float L = 0.f, A = 0.f;
-      if (M != -INFINITY) {
-#pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) {
-          const float f = safe_exp2_diff(sm_m[w][r], M);
-          L += sm_l[w][r] * f;
-          A += sm_acc[w][r][d] * f;
-        }
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      if (qr < REP) {
+        qa[kk][0] = *reinterpret_cast<const uint32_t*>(qrow_ptr + kk * 16 + 2 * qt);
+        qa[kk][1] = *reinterpret_cast<const uint32_t*>(qrow_ptr + kk * 16 + 8 + 2 * qt);
+      } else {
+        qa[kk][0] = qa[kk][1] = 0u;
       }
-      if (npad > 0) {
-        const float Mp = fmaxf(M, 0.f);
-        const float f = M == -INFINITY ? 0.f : exp2f(M - Mp);
-        L = L * f + (float)npad * exp2f(-Mp);
-        A = A * f;
-      }
-      outp[i] = from_f32<T>(L > 0.f ? A / L : 0.f);
     }
-    return;
   }
 
-  // Write this split's partial state, then let the last split of (row, g) merge.
-  for (int i = threadIdx.x; i < REP * HD; i += blockDim.x) {
-    const int r = i / HD, d = i % HD;
-    float M = -INFINITY;
+  const int64_t tok_stride_b = (int64_t)p.nkv * HD * 2;  // bytes between token rows of the pool
+  const char* kbase = reinterpret_cast<const char*>(p.k_cache) + (p.layer_off + (int64_t)g * HD) * 2;
+  const char* vbase = reinterpret_cast<const char*>(p.v_cache) + (p.layer_off + (int64_t)g * HD) * 2;
+  const uint32_t wsm = smem_addr(smem) + (uint32_t)(warp * kMmaStages * C::STAGEB);
+
+  // Issue the copies of this warp's i-th block into ring slot (i % STAGES); returns false
+  // for a block id outside the pool (its scores are then masked).
+  auto issue = [&](int i) {
+    const int blk = table[blk0 + warp + i * kMmaWarps];
+    if (blk < 0 || blk >= p.num_blocks) return;
+    const uint32_t st = wsm + (uint32_t)((i % kMmaStages) * C::STAGEB);
+    const int64_t blk_off = (int64_t)blk * bs * tok_stride_b;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w][r]);
-    float L = 0.f, A = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) {
-        const float f = safe_exp2_diff(sm_m[w][r], M);
-        L += sm_l[w][r] * f;
-        A += sm_acc[w][r][d] * f;
-      }
+    for (int q = lane; q < 16 * C::CHUNKS; q += 32) {
+      const int r = q / C::CHUNKS, c = q % C::CHUNKS;
+      const int64_t src = blk_off + r * tok_stride_b + c * 16;
+      cp_async16(st + swz<HD>(r, c), kbase + src);
+      cp_async16(st + C::BLKB + swz<HD>(r, c), vbase + src);
     }
-    const int64_t h = head0 + r;
-    p.ws_o[(h * p.splits + split) * HD + d] = A;
-    if (d == 0) {
-      p.ws_ml[(h * p.splits + split) * 2 + 0] = M;
-      p.ws_ml[(h * p.splits + split) * 2 + 1] = L;
+  };
+
+  float o[HD / 8][4];
+#pragma unroll
+  for (int d = 0; d < HD / 8; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;  // row qr statistics (per-lane partial l)
+
+#pragma unroll
+  for (int i = 0; i < kMmaStages - 1; ++i) {
+    if (i < n_w) issue(i);
+    cp_async_commit();
+  }
+  for (int i = 0; i < n_w; ++i) {
+    if (i + kMmaStages - 1 < n_w) issue(i + kMmaStages - 1);
+    cp_async_commit();
+    cp_async_wait<kMmaStages - 1>();
+    __syncwarp();
+    const int bidx = blk0 + warp + i * kMmaWarps;
+    const int blk = table[bidx];
+    const bool blk_ok = blk >= 0 && blk < p.num_blocks;
+    if (!blk_ok && lane == 0) raise_status(p.status, B2_DEV_RANGE);
+    const uint32_t ks = wsm + (uint32_t)((i % kMmaStages) * C::STAGEB);
+    const uint32_t vs = ks + C::BLKB;
+
+    // S = Q K^T over 16 tokens: two 8-token n-tiles.
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      // matrices: (tokens 0-7, dims lo), (tokens 0-7, dims hi), (tokens 8-15, lo), (tokens 8-15, hi)
+      const int mrow = (lane & 7) + ((lane >> 4) << 3);
+      const int mchunk = kk * 2 + ((lane >> 3) & 1);
+      uint32_t b[4];
+      ldsm_x4(ks + swz<HD>(mrow, mchunk), b);
+      mma_bf16(s[0], qa[kk][0], 0u, qa[kk][1], 0u, b[0], b[1]);
+      mma_bf16(s[1], qa[kk][0], 0u, qa[kk][1], 0u, b[2], b[3]);
+    }
+    // scale, mask, online softmax on row qr (accumulator elements 0, 1 of each n-tile)
+    const int tbase = bidx * bs;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = tbase + j * 8 + 2 * qt + e;
+        const float v = (blk_ok && t < ctx) ? s[j][e] * p.scale_log2 : -INFINITY;
+        s[j][e] = v;
+        mx = fmaxf(mx, v);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float corr = safe_exp2_diff(m_run, m_new);
+    float pv[2][2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) pv[j][e] = m_new == -INFINITY ? 0.f : safe_exp2_diff(s[j][e], m_new);
+    l_run = l_run * corr + (pv[0][0] + pv[0][1] + pv[1][0] + pv[1][1]);
+    m_run = m_new;
+#pragma unroll
+    for (int d = 0; d < HD / 8; ++d) {
+      o[d][0] *= corr;
+      o[d][1] *= corr;
+    }
+    // P as the A operand (rows 8..15 zero), O += P V
+    const uint32_t pa0 = pack_bf16(pv[0][0], pv[0][1]);
+    const uint32_t pa2 = pack_bf16(pv[1][0], pv[1][1]);
+#pragma unroll
+    for (int d = 0; d < HD / 8; d += 2) {
+      // matrices: (tokens 0-7, dims 8d), (tokens 8-15, dims 8d), (tokens 0-7, 8d+8), (tokens 8-15, 8d+8)
+      const int mrow = (lane & 7) + (((lane >> 3) & 1) << 3);
+      const int mchunk = d + (lane >> 4);
+      uint32_t b[4];
+      ldsm_x4_trans(vs + swz<HD>(mrow, mchunk), b);
+      mma_bf16(o[d], pa0, 0u, pa2, 0u, b[0], b[1]);
+      mma_bf16(o[d + 1], pa0, 0u, pa2, 0u, b[2], b[3]);
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  __syncthreads();  // the rings are idle; reuse them for the merge arrays
+
+  float* sm_m = reinterpret_cast<float*>(smem);
+  float* sm_l = sm_m + kMmaWarps * REP;
+  float* sm_acc = sm_l + kMmaWarps * REP;
+  if (qr < REP) {
+    if (qt == 0) {
+      sm_m[warp * REP + qr] = m_run;
+      sm_l[warp * REP + qr] = l_run;
+    }
+#pragma unroll
+    for (int d = 0; d < HD / 8; ++d) {
+      sm_acc[(warp * REP + qr) * HD + d * 8 + 2 * qt] = o[d][0];
+      sm_acc[(warp * REP + qr) * HD + d * 8 + 2 * qt + 1] = o[d][1];
     }
   }
-  __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int* ctr = p.counters + (int64_t)row * p.nkv + g;
-    const int prev = atomicAdd(ctr, 1);
-    const int last = prev == p.splits - 1;
-    if (last) *ctr = 0;  // ready for the next launch
-    sm_flag = last;
+  attn_finalize<__nv_bfloat16, HD, REP>(p, sm_m, sm_l, sm_acc, kMmaWarps, row, g, split, ctx);
+}
+
+template <int HD>
+static int launch_mma_rep(int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {
+  using C = MmaCfg<HD>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto set = [&](const void* fn) -> int {
+    if (dev >= 0 && dev < 64 && !attr_set[dev] && C::SMEM > 48 * 1024)
+      B2_TRY_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+    return B2_OK;
+  };
+  int rc = B2_OK;
+  switch (rep) {
+    case 1: rc = set((const void*)paged_attn_mma_kernel<HD, 1>); if (!rc) paged_attn_mma_kernel<HD, 1><<<grid, kMmaWarps * 32, C::SMEM, s>>>(p); break;
+    case 2: rc = set((const void*)paged_attn_mma_kernel<HD, 2>); if (!rc) paged_attn_mma_kernel<HD, 2><<<grid, kMmaWarps * 32, C::SMEM, s>>>(p); break;
+    case 4: rc = set((const void*)paged_attn_mma_kernel<HD, 4>); if (!rc) paged_attn_mma_kernel<HD, 4><<<grid, kMmaWarps * 32, C::SMEM, s>>>(p); break;
+    case 8: rc = set((const void*)paged_attn_mma_kernel<HD, 8>); if (!rc) paged_attn_mma_kernel<HD, 8><<<grid, kMmaWarps * 32, C::SMEM, s>>>(p); break;
+    default: return fail(B2_ENOTSUP, "b2_paged_attention: nq/nkv = %d not supported (1, 2, 4, 8)", rep);
   }
-  __syncthreads();
-  if (!sm_flag) return;
-  __threadfence();
-  for (int i = threadIdx.x; i < REP * HD; i += blockDim.x) {
-    const int r = i / HD, d = i % HD;
-    const int64_t h = head0 + r;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, __ldcg(&p.ws_ml[(h * p.splits + s2) * 2]));
-    float L = 0.f, A = 0.f;
-    if (M != -INFINITY) {
-      for (int s2 = 0; s2 < p.splits; ++s2) {
-        const float f = safe_exp2_diff(__ldcg(&p.ws_ml[(h * p.splits + s2) * 2]), M);
-        L += __ldcg(&p.ws_ml[(h * p.splits + s2) * 2 + 1]) * f;
-        A += __ldcg(&p.ws_o[(h * p.splits + s2) * HD + d]) * f;
-      }
-    }
-    if (npad > 0) {
-      const float Mp = fmaxf(M, 0.f);
-      const float f = M == -INFINITY ? 0.f : exp2f(M - Mp);
-      L = L * f + (float)npad * exp2f(-Mp);
-      A = A * f;
-    }
-    outp[i] = from_f32<T>(L > 0.f ? A / L : 0.f);
+  if (rc) return rc;
+  B2_TRY_CUDA(cudaGetLastError());
+  return B2_OK;
+}
+
+static int launch_mma(int hd, int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {
+  switch (hd) {
+    case 32: return launch_mma_rep<32>(rep, p, grid, s);
+    case 64: return launch_mma_rep<64>(rep, p, grid, s);
+    case 128: return launch_mma_rep<128>(rep, p, grid, s);
+    default: return fail(B2_ENOTSUP, "b2_paged_attention: bf16 head_dim %d not supported (32, 64, 128)", hd);
   }
 }
 
@@ -428,7 +690,10 @@ int b2_paged_attention(const void* q, int64_t ld_q, int n_rows, int nq, int nkv,
   p.status = status;
   dim3 grid(num_splits, nkv, n_rows);
   const int rep = nq / nkv;
-  if (dtype == B2_BF16) return b2::launch_hd<__nv_bfloat16>(head_dim, rep, p, grid, stream);
+  if (dtype == B2_BF16) {
+    B2_CHECK_ARG(block_size == 16, "b2_paged_attention: bf16 path needs block_size 16");
+    return b2::launch_mma(head_dim, rep, p, grid, stream);
+  }
   return b2::launch_hd<float>(head_dim, rep, p, grid, stream);
 }
 

@@ -492,8 +492,6 @@ static Plan make_plan(int M, int n_tiles, int K) {
   return pl;
 }
 
-static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
-
 // Workspace layout: a FIXED-size counter region (so that launches of different tile
 // counts never see each other's partial tiles as counters), then the partial tiles.
 constexpr size_t kCounterSlots = 65536;
