@@ -17,6 +17,8 @@
 //  * compat_pad reproduces the reference's unmasked zero padding
 //    (attention.py:190-203): (max_ctx - ctx) extra keys with score 0 and value 0.
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "common.cuh"
 
@@ -526,17 +528,23 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnP
   attn_finalize<__nv_bfloat16, HD, REP>(p, sm_m, sm_l, sm_acc, kMmaWarps, row, g, split, ctx);
 }
 
+// Opts a kernel into `bytes` of dynamic shared memory once per (kernel, device).
+static int allow_dynamic_smem(const void* fn, size_t bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  B2_TRY_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({fn, dev})) return B2_OK;
+  B2_TRY_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  done.insert({fn, dev});
+  return B2_OK;
+}
+
 template <int HD>
 static int launch_mma_rep(int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {
   using C = MmaCfg<HD>;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  auto set = [&](const void* fn) -> int {
-    if (dev >= 0 && dev < 64 && !attr_set[dev] && C::SMEM > 48 * 1024)
-      B2_TRY_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
-    return B2_OK;
-  };
+  auto set = [&](const void* fn) -> int { return allow_dynamic_smem(fn, C::SMEM); };
   int rc = B2_OK;
   switch (rep) {
     case 1: rc = set((const void*)paged_attn_mma_kernel<HD, 1>); if (!rc) paged_attn_mma_kernel<HD, 1><<<grid, kMmaWarps * 32, C::SMEM, s>>>(p); break;
