@@ -30,7 +30,7 @@ namespace tc {
 
 constexpr int BM = 128;  // weight rows per tile (MMA M)
 constexpr int BK = 64;   // K elements per stage = one 128-byte swizzle atom
-constexpr int kThreads = 128;
+constexpr int kThreads = 192;  // 6 warps: producer, MMA, 4 epilogue
 constexpr int kMaxSegs = 3;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on any pipeline wait
 
@@ -169,55 +169,90 @@ __host__ __device__ constexpr uint32_t instr_desc_bf16(int m, int n) {
          | ((uint32_t)(m >> 4) << 24);    // M / 16
 }
 
-template <int BN>
+// Named barrier over the four epilogue warps only (the producer and MMA warps keep running).
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// AND of `pred` over the four epilogue warps (a barrier among them, like epilogue_sync).
+__device__ __forceinline__ bool epilogue_all(bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"((uint32_t)pred)
+      : "memory");
+  return out != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int BN, bool SWIGLU>
 struct Cfg {
-  static constexpr uint32_t A_BYTES = BM * BK * 2;
-  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t A_BYTES = (SWIGLU ? 2 : 1) * BM * BK * 2;  // gate (+ up) weight tiles
+  static constexpr uint32_t B_BYTES = BN * BK * 2;                      // activation tile
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
-  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
+  static constexpr uint32_t ACC_COLS = (SWIGLU ? 2 : 1) * BN;           // TMEM columns per accumulator
+  static constexpr int NBUF = 2 * ACC_COLS <= 512 ? 2 : 1;              // double-buffered accumulators
+  static constexpr uint32_t TMEM_COLS = NBUF * ACC_COLS < 32 ? 32 : NBUF * ACC_COLS;
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024;
+  static_assert(STAGES >= 2, "pipeline too shallow");
+  static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS <= 512, "TMEM allocation must be a power of 2");
 };
 
-template <int BN>
+// Unit u -> (split, tile, m tile); the splits of one tile are consecutive units, so
+// persistent CTAs working side by side finish a tile's splits at about the same time.
+struct Unit {
+  int split, tile, mt;
+};
+__device__ __forceinline__ Unit decode_unit(const Params& p, int u) {
+  Unit w;
+  w.split = u % p.splits;
+  const int rest = u / p.splits;
+  w.tile = rest % p.n_tiles;
+  w.mt = rest / p.n_tiles;
+  return w;
+}
+
+// Persistent warp-specialised kernel: warp 0 = TMA producer, warp 1 = MMA issuer and
+// TMEM owner, warps 2-5 = epilogue (TMEM lane quarter = warp % 4).
+template <int BN, bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW0,
                    const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmW2,
                    const Params p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, SWIGLU>;
   constexpr int STAGES = C::STAGES;
+  constexpr int NBUF = C::NBUF;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t done_bar;
+  __shared__ __align__(8) uint64_t acc_full[NBUF];
+  __shared__ __align__(8) uint64_t acc_empty[NBUF];
+  __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ int s_last;
 
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  const int tile = blockIdx.x, mt = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Constant indices only: a dynamically indexed parameter array would be copied
-  // to local memory.
-  int seg = 0;
-  if (p.nseg > 1 && tile >= p.seg_tile_start[1]) seg = 1;
-  if (p.nseg > 2 && tile >= p.seg_tile_start[2]) seg = 2;
-  const int local_tile = tile - (seg == 0 ? p.seg_tile_start[0] : seg == 1 ? p.seg_tile_start[1] : p.seg_tile_start[2]);
-  const int seg_n = seg == 0 ? p.seg_n[0] : seg == 1 ? p.seg_n[1] : p.seg_n[2];
-  const int seg_col = seg == 0 ? p.seg_col[0] : seg == 1 ? p.seg_col[1] : p.seg_col[2];
-  const int kb0 = split * p.kb_per_split;
-  const int kb1 = min(p.nkb, kb0 + p.kb_per_split);
-  const int nk = kb1 - kb0;
-  const int m0 = mt * BN;
+  const int units = p.n_tiles * p.m_tiles * p.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&done_bar, 1);
+    for (int b = 0; b < NBUF; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(&drain_bar, 1);
     fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == 1) {
     tmem_alloc(&tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -226,206 +261,221 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
 
-  int issued = 0;
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer
-    const uint64_t pol_w = policy_evict_first();
-    const uint64_t pol_x = policy_evict_last();
-    for (int i = 0; i < nk; ++i) {
-      const int st = i % STAGES;
-      const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-      if (!mbar_wait(&empty_bar[st], ph ^ 1u)) {
-        raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
-        break;
+  if (warp == 0) {
+    // ---------------- TMA producer (one lane)
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit w = decode_unit(p, u);
+        int seg = 0;
+        if (p.nseg > 1 && w.tile >= p.seg_tile_start[1]) seg = 1;
+        if (p.nseg > 2 && w.tile >= p.seg_tile_start[2]) seg = 2;
+        const int local_tile = w.tile - (seg == 0 ? p.seg_tile_start[0] : seg == 1 ? p.seg_tile_start[1]
+                                                                                    : p.seg_tile_start[2]);
+        const int kb0 = w.split * p.kb_per_split;
+        const int kb1 = min(p.nkb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int st = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!mbar_wait(&empty_bar[st], ph ^ 1u)) {
+            raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + (size_t)st * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[st], C::STAGE_BYTES);
+          const int kx = kb * BK;
+          if (SWIGLU) {
+            tma_load_2d(sa, &tmW0, &full_bar[st], kx, local_tile * BM, pol_w);
+            tma_load_2d(sa + BM * BK * 2, &tmW1, &full_bar[st], kx, local_tile * BM, pol_w);
+          } else if (seg == 0) {  // descriptors are addressed in param space, never copied
+            tma_load_2d(sa, &tmW0, &full_bar[st], kx, local_tile * BM, pol_w);
+          } else if (seg == 1) {
+            tma_load_2d(sa, &tmW1, &full_bar[st], kx, local_tile * BM, pol_w);
+          } else {
+            tma_load_2d(sa, &tmW2, &full_bar[st], kx, local_tile * BM, pol_w);
+          }
+          tma_load_2d(sb, &tmX, &full_bar[st], kx, w.mt * BN, pol_x);
+        }
       }
-      uint8_t* sa = smem + (size_t)st * C::STAGE_BYTES;
-      uint8_t* sb = sa + C::A_BYTES;
-      mbar_arrive_expect_tx(&full_bar[st], C::STAGE_BYTES);
-      const int kx = (kb0 + i) * BK;
-      if (p.epi == kEpiSwiglu) {
-        tma_load_2d(sa, &tmW0, &full_bar[st], kx, local_tile * 64, pol_w);
-        tma_load_2d(sa + C::A_BYTES / 2, &tmW1, &full_bar[st], kx, local_tile * 64, pol_w);
-      } else if (seg == 0) {  // descriptors are addressed in param space, never copied
-        tma_load_2d(sa, &tmW0, &full_bar[st], kx, local_tile * BM, pol_w);
-      } else if (seg == 1) {
-        tma_load_2d(sa, &tmW1, &full_bar[st], kx, local_tile * BM, pol_w);
-      } else {
-        tma_load_2d(sa, &tmW2, &full_bar[st], kx, local_tile * BM, pol_w);
+      // Copies still in flight (only after an aborted pipeline) land before the CTA exits.
+      for (int st = 0; st < STAGES && st < it; ++st) {
+        const int last_i = st + ((it - 1 - st) / STAGES) * STAGES;
+        mbar_wait(&full_bar[st], (uint32_t)(last_i / STAGES) & 1u, 100000000ull);
       }
-      tma_load_2d(sb, &tmX, &full_bar[st], kx, m0, pol_x);
-      ++issued;
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
-    constexpr uint32_t idesc = instr_desc_bf16(BM, BN);
-    for (int i = 0; i < nk; ++i) {
-      const int st = i % STAGES;
-      const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-      if (!mbar_wait(&full_bar[st], ph)) {
-        raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (one lane)
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc_bf16(BM, BN);
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++j) {
+        const Unit w = decode_unit(p, u);
+        const int buf = j % NBUF;
+        const uint32_t acc = tmem + (uint32_t)(buf * C::ACC_COLS);
+        if (!mbar_wait(&acc_empty[buf], ((uint32_t)(j / NBUF) & 1u) ^ 1u)) {
+          raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+        const int kb0 = w.split * p.kb_per_split;
+        const int kb1 = min(p.nkb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int st = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!mbar_wait(&full_bar[st], ph)) {
+            raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + (size_t)st * C::STAGE_BYTES);
+          const uint64_t adesc = smem_desc_sw128(a_addr);
+          const uint64_t bdesc = smem_desc_sw128(a_addr + C::A_BYTES);
+          const uint32_t first = kb == kb0 ? 1u : 0u;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)  // +32 bytes along K per MMA = +2 in the address field
+            umma_bf16(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
+          if (SWIGLU) {
+            const uint64_t udesc = smem_desc_sw128(a_addr + BM * BK * 2);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              umma_bf16(acc + BN, udesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
+          }
+          umma_commit(&empty_bar[st]);
+        }
+        umma_commit(&acc_full[buf]);
+      }
+      // Every MMA issued by this thread has completed once drain_bar fires.
+      umma_commit(&drain_bar);
+      mbar_wait(&drain_bar, 0, 100000000ull);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue warps 2-5
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // accumulator row = TMEM lane
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int M = p.M;
+    int j = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+      const Unit w = decode_unit(p, u);
+      int seg = 0;
+      if (p.nseg > 1 && w.tile >= p.seg_tile_start[1]) seg = 1;
+      if (p.nseg > 2 && w.tile >= p.seg_tile_start[2]) seg = 2;
+      const int local_tile = w.tile - (seg == 0 ? p.seg_tile_start[0] : seg == 1 ? p.seg_tile_start[1]
+                                                                                  : p.seg_tile_start[2]);
+      const int seg_n = seg == 0 ? p.seg_n[0] : seg == 1 ? p.seg_n[1] : p.seg_n[2];
+      const int seg_col = seg == 0 ? p.seg_col[0] : seg == 1 ? p.seg_col[1] : p.seg_col[2];
+      const int buf = j % NBUF;
+      const uint32_t acc = tmem + lane_base + (uint32_t)(buf * C::ACC_COLS);
+      const int m0 = w.mt * BN;
+      const int ncols = min(BN, M - m0);
+      const int n = local_tile * BM + r;
+      const bool nok = n < seg_n;
+      // Uniform verdict: the split-K path below meets at named barriers.
+      const bool done = epilogue_all(mbar_wait(&acc_full[buf], (uint32_t)(j / NBUF) & 1u));
+      if (!done) {
+        if (lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
         break;
       }
       tc_fence_after();
-      const uint32_t a_addr = smem_u32(smem + (size_t)st * C::STAGE_BYTES);
-      const uint64_t adesc = smem_desc_sw128(a_addr);
-      const uint64_t bdesc = smem_desc_sw128(a_addr + C::A_BYTES);
+      if (p.splits == 1) {
+        const int64_t col = (int64_t)seg_col + n;
+        const float bv = (nok && p.bias) ? p.bias[col] : 0.f;
+        for (int c0 = 0; c0 < ncols; c0 += 16) {
+          float v[16];
+          tmem_ld16(acc + c0, v);
+          if (SWIGLU) {
+            float uv[16];
+            tmem_ld16(acc + BN + c0, uv);
 #pragma unroll
-      for (int kk = 0; kk < BK / 16; ++kk)  // +32 bytes along K per MMA = +2 in the address field
-        umma_bf16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
-      umma_commit(&empty_bar[st]);
-    }
-    umma_commit(&done_bar);
-  }
-  __syncwarp();
-
-  // ---------------- epilogue
-  // Block-uniform verdict so that the epilogue's barriers are reached by all threads.
-  const bool done = __syncthreads_and(mbar_wait(&done_bar, 0)) != 0;
-  tc_fence_after();
-  if (!done && threadIdx.x == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
-  const int r = warp * 32 + lane;  // accumulator row = TMEM lane
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-  const int M = p.M;
-
-  if (done && p.splits == 1) {
-    if (p.epi == kEpiStore) {
-      const int n = local_tile * BM + r;
-      const bool nok = n < seg_n;
-      const int64_t col = (int64_t)seg_col + n;
-      const float bv = (nok && p.bias) ? p.bias[col] : 0.f;
-      for (int c0 = 0; c0 < BN && m0 + c0 < M; c0 += 16) {
-        float v[16];
-        tmem_ld16(trow + c0, v);
-        if (nok) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = m0 + c0 + j;
-            if (m < M) st_dyn(p.y, p.y_dtype, (int64_t)m * p.ldy + col, v[j] + bv);
+            for (int e = 0; e < 16; ++e) v[e] = silu_f32(v[e]) * uv[e];
           }
-        }
-      }
-    } else {
-      // SwiGLU: TMEM lanes 0-63 hold gate rows, 64-127 the matching up rows.
-      float* su = reinterpret_cast<float*>(smem);  // [BN][64], pipeline buffers are idle now
-      if (warp >= 2) {
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          float v[16];
-          tmem_ld16(trow + c0, v);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) su[(c0 + j) * 64 + (r - 64)] = v[j];
-        }
-      }
-      __syncthreads();
-      if (warp < 2) {
-        const int n = local_tile * 64 + r;
-        const bool nok = n < p.seg_n[0];
-        for (int c0 = 0; c0 < BN && m0 + c0 < M; c0 += 16) {
-          float v[16];
-          tmem_ld16(trow + c0, v);
           if (nok) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int m = m0 + c0 + j;
-              if (m < M) st_dyn(p.y, p.y_dtype, (int64_t)m * p.ldy + n, silu_f32(v[j]) * su[(c0 + j) * 64 + r]);
-            }
+            for (int e = 0; e < 16; ++e)
+              if (c0 + e < ncols) st_dyn(p.y, p.y_dtype, (int64_t)(m0 + c0 + e) * p.ldy + col, v[e] + bv);
           }
         }
-      }
-    }
-  } else if (done) {
-    // Split-K: publish this split's float32 tile, the last split reduces.
-    const int64_t tile_elems = (int64_t)BM * BN;
-    const int64_t slot = (int64_t)tile * p.m_tiles + mt;
-    float* mine = p.ws + ((int64_t)split * p.n_tiles * p.m_tiles + slot) * tile_elems;
-    for (int c0 = 0; c0 < BN && m0 + c0 < M; c0 += 16) {
-      float v[16];
-      tmem_ld16(trow + c0, v);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      } else {
+        // Split-K: publish this split's float32 tile ([column][128 rows], gate then up for
+        // SwiGLU), release TMEM, and let the last split of the tile reduce.
+        constexpr int PARTS = SWIGLU ? 2 : 1;
+        const int64_t tile_elems = (int64_t)PARTS * BM * BN;
+        const int64_t slot = (int64_t)w.tile * p.m_tiles + w.mt;
+        float* mine = p.ws + ((int64_t)w.split * p.n_tiles * p.m_tiles + slot) * tile_elems;
+        for (int c0 = 0; c0 < ncols; c0 += 16) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) mine[(int64_t)(c0 + j) * BM + r] = v[j];
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int* ctr = p.counters + slot;
-      const int prev = atomicAdd(ctr, 1);
-      s_last = prev == p.splits - 1;
-      if (s_last) *ctr = 0;
-    }
-    __syncthreads();
-    if (s_last) {
-      __threadfence();
-      const int64_t split_stride = (int64_t)p.n_tiles * p.m_tiles * tile_elems;
-      const float* base = p.ws + slot * tile_elems;
-      const int ncols = min(BN, M - m0);
-      const int nsplit = p.splits;
-      if (p.epi == kEpiStore) {
-        // Each warp reduces whole token columns (128 contiguous floats = 32 lanes x float4),
-        // 4 columns per pass with every split's loads issued before any store.
-        const int r4 = lane * 4;
-        const int n0 = local_tile * BM + r4;
-        float bv[4];
+          for (int part = 0; part < PARTS; ++part) {
+            float v[16];
+            tmem_ld16(acc + part * BN + c0, v);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) bv[e] = (p.bias && n0 + e < seg_n) ? p.bias[seg_col + n0 + e] : 0.f;
-        for (int cb = warp * 4; cb < ncols; cb += 16) {
-          float4 acc[4];
+            for (int e = 0; e < 16; ++e) mine[((int64_t)part * BN + c0 + e) * BM + r] = v[e];
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        __threadfence();
+        epilogue_sync();
+        if (threadIdx.x == 64) {
+          int* ctr = p.counters + slot;
+          const int prev = atomicAdd(ctr, 1);
+          s_last = prev == p.splits - 1;
+          if (s_last) *ctr = 0;
+        }
+        epilogue_sync();
+        if (s_last) {
+          __threadfence();
+          const int64_t split_stride = (int64_t)p.n_tiles * p.m_tiles * tile_elems;
+          const float* base = p.ws + slot * tile_elems;
+          // Each epilogue warp reduces whole token columns: 32 lanes x float4 = 128 rows.
+          const int r4 = lane * 4;
+          const int nb = local_tile * BM + r4;
+          float bv[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int sp = 0; sp < nsplit; ++sp) {
-            const float* src = base + sp * split_stride + r4;
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              if (cb + u < ncols) {
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(src + (int64_t)(cb + u) * BM));
-                acc[u].x += v.x; acc[u].y += v.y; acc[u].z += v.z; acc[u].w += v.w;
+          for (int e = 0; e < 4; ++e) bv[e] = (!SWIGLU && p.bias && nb + e < seg_n) ? p.bias[seg_col + nb + e] : 0.f;
+          for (int c = quarter; c < ncols; c += 4) {
+            float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), u4 = g4;
+            for (int sp = 0; sp < p.splits; ++sp) {
+              const float* src = base + sp * split_stride + (int64_t)c * BM + r4;
+              const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
+              g4.x += a.x; g4.y += a.y; g4.z += a.z; g4.w += a.w;
+              if (SWIGLU) {
+                const float4 b = __ldcg(reinterpret_cast<const float4*>(src + (int64_t)BN * BM));
+                u4.x += b.x; u4.y += b.y; u4.z += b.z; u4.w += b.w;
               }
             }
-          }
+            const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+            const float uv[4] = {u4.x, u4.y, u4.z, u4.w};
+            const int64_t rowoff = (int64_t)(m0 + c) * p.ldy + seg_col;
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (cb + u >= ncols) continue;
-            const int64_t rowoff = (int64_t)(m0 + cb + u) * p.ldy + seg_col;
-            const float vals[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (n0 + e < seg_n) st_dyn(p.y, p.y_dtype, rowoff + n0 + e, vals[e] + bv[e]);
+            for (int e = 0; e < 4; ++e) {
+              if (nb + e >= seg_n) continue;
+              const float val = SWIGLU ? silu_f32(gv[e]) * uv[e] : gv[e] + bv[e];
+              st_dyn(p.y, p.y_dtype, rowoff + nb + e, val);
+            }
           }
         }
-      } else {
-        // SwiGLU: lanes 0-15 / 16-31 take two token columns; each lane holds 4 gate rows
-        // (TMEM lanes 0-63 of the tile) and the matching 4 up rows (64-127).
-        const int half = lane >> 4;
-        const int r4 = (lane & 15) * 4;
-        const int n0 = local_tile * 64 + r4;
-        for (int cb = warp * 2 + half; cb < ncols; cb += 8) {
-          float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), us = gs;
-          for (int sp = 0; sp < nsplit; ++sp) {
-            const float* src = base + sp * split_stride + (int64_t)cb * BM + r4;
-            const float4 gv = __ldcg(reinterpret_cast<const float4*>(src));
-            const float4 uv = __ldcg(reinterpret_cast<const float4*>(src + 64));
-            gs.x += gv.x; gs.y += gv.y; gs.z += gv.z; gs.w += gv.w;
-            us.x += uv.x; us.y += uv.y; us.z += uv.z; us.w += uv.w;
-          }
-          const int64_t rowoff = (int64_t)(m0 + cb) * p.ldy;
-          const float g4[4] = {gs.x, gs.y, gs.z, gs.w}, u4[4] = {us.x, us.y, us.z, us.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (n0 + e < seg_n) st_dyn(p.y, p.y_dtype, rowoff + n0 + e, silu_f32(g4[e]) * u4[e]);
-        }
+        epilogue_sync();  // s_last is rewritten by the next unit
       }
     }
   }
 
   // ---------------- teardown
-  if (warp == 0 && lane == 0) {
-    // Copies still in flight after an aborted pipeline land before the CTA exits.
-    for (int st = 0; st < STAGES && st < issued; ++st) {
-      const int last_i = st + ((issued - 1 - st) / STAGES) * STAGES;
-      mbar_wait(&full_bar[st], (uint32_t)(last_i / STAGES) & 1u, 100000000ull);
-    }
-  }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
@@ -461,34 +511,36 @@ static int make_map(CUtensorMap* m, const void* ptr, uint64_t k, uint64_t rows, 
 }
 
 struct Plan {
-  int BN, m_tiles, n_tiles, nkb, splits, kbps;
+  int BN, m_tiles, n_tiles, nkb, splits, kbps, ctas;
 };
 
-static Plan make_plan(int M, int n_tiles, int K) {
+// Split-K choice for the persistent kernel: each CTA streams ceil(units / SMs) units of
+// kbps k-blocks; split-K adds one float32 partial tile write per unit and a reduction
+// of all partials by the tile's last split.  Costs are bytes through one SM.
+static Plan make_plan(int M, int n_tiles, int K, bool swiglu) {
   Plan pl{};
   pl.BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
   pl.m_tiles = (M + pl.BN - 1) / pl.BN;
   pl.n_tiles = n_tiles;
   pl.nkb = (K + BK - 1) / BK;
-  // Cost in bytes moved through one SM on the critical path: every wave streams
-  // kbps stages; with split-K each CTA also writes a float32 partial tile and the
-  // last CTA of a tile reads all of them back.
   const int sms = sm_count();
-  const long units = (long)n_tiles * pl.m_tiles;
-  const long stage = (long)(BM + pl.BN) * BK * 2;
-  const long partial = (long)BM * pl.BN * 4;
+  const long tiles = (long)n_tiles * pl.m_tiles;
+  const long stage = (long)((swiglu ? 2 : 1) * BM + pl.BN) * BK * 2;
+  const long partial = (long)(swiglu ? 2 : 1) * BM * pl.BN * 4;
   long best_cost = -1;
   for (int s = 1; s <= 16 && s <= pl.nkb; ++s) {
     const int kbps = (pl.nkb + s - 1) / s;
     const int s_eff = (pl.nkb + kbps - 1) / kbps;
-    const long waves = (units * s_eff + sms - 1) / sms;
-    const long cost = waves * (kbps * stage + (s_eff > 1 ? partial : 0)) + (s_eff > 1 ? s_eff * partial : 0);
+    const long per_cta = (tiles * s_eff + sms - 1) / sms;
+    const long cost = per_cta * (kbps * stage + (s_eff > 1 ? partial : 0)) + (s_eff > 1 ? s_eff * partial : 0);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       pl.splits = s_eff;
       pl.kbps = kbps;
     }
   }
+  const long units = tiles * pl.splits;
+  pl.ctas = (int)(units < sms ? units : sms);
   return pl;
 }
 
@@ -497,47 +549,61 @@ static Plan make_plan(int M, int n_tiles, int K) {
 constexpr size_t kCounterSlots = 65536;
 constexpr size_t kCounterBytes = kCounterSlots * sizeof(int);
 
-static size_t plan_ws_bytes(const Plan& pl) {
+static size_t plan_ws_bytes(const Plan& pl, bool swiglu) {
   if (pl.splits <= 1) return 0;
-  const size_t units = (size_t)pl.n_tiles * pl.m_tiles;
-  return kCounterBytes + (size_t)pl.splits * units * BM * pl.BN * sizeof(float);
+  const size_t tiles = (size_t)pl.n_tiles * pl.m_tiles;
+  return kCounterBytes + (size_t)pl.splits * tiles * (swiglu ? 2 : 1) * BM * pl.BN * sizeof(float);
 }
 
-template <int BN>
+template <int BN, bool SWIGLU>
 static int launch(const CUtensorMap& mx, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& w2,
-                  const Params& p, dim3 grid, cudaStream_t s) {
-  using C = Cfg<BN>;
+                  const Params& p, int ctas, cudaStream_t s) {
+  using C = Cfg<BN, SWIGLU>;
   static bool attr_set[64] = {false};
   int dev = 0;
-  cudaGetDevice(&dev);
+  B2_TRY_CUDA(cudaGetDevice(&dev));
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    B2_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+    B2_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)C::SMEM));
     attr_set[dev] = true;
   }
-  gemm_tc_kernel<BN><<<grid, kThreads, C::SMEM, s>>>(mx, w0, w1, w2, p);
+  gemm_tc_kernel<BN, SWIGLU><<<ctas, kThreads, C::SMEM, s>>>(mx, w0, w1, w2, p);
   B2_TRY_CUDA(cudaGetLastError());
   return B2_OK;
+}
+
+template <bool SWIGLU>
+static int launch_bn(int BN, const CUtensorMap& mx, const CUtensorMap* mw, const Params& p, int ctas,
+                     cudaStream_t s) {
+  switch (BN) {
+    case 16: return launch<16, SWIGLU>(mx, mw[0], mw[1], mw[2], p, ctas, s);
+    case 32: return launch<32, SWIGLU>(mx, mw[0], mw[1], mw[2], p, ctas, s);
+    case 64: return launch<64, SWIGLU>(mx, mw[0], mw[1], mw[2], p, ctas, s);
+    case 128: return launch<128, SWIGLU>(mx, mw[0], mw[1], mw[2], p, ctas, s);
+    default: return launch<256, SWIGLU>(mx, mw[0], mw[1], mw[2], p, ctas, s);
+  }
 }
 
 }  // namespace tc
 
 static int tc_tiles(const GemmSeg* segs, int nseg, int epi, int* starts) {
   int total = 0;
-  for (int i = 0; i < nseg; ++i) {
+  const int n_used = epi == kEpiSwiglu ? 1 : nseg;
+  for (int i = 0; i < n_used; ++i) {
     starts[i] = total;
-    total += epi == kEpiSwiglu ? (segs[0].n + 63) / 64 : (segs[i].n + tc::BM - 1) / tc::BM;
-    if (epi == kEpiSwiglu) break;
+    total += (segs[i].n + tc::BM - 1) / tc::BM;
   }
-  starts[epi == kEpiSwiglu ? 1 : nseg] = total;
+  for (int i = n_used; i <= tc::kMaxSegs; ++i) starts[i] = total;
   return total;
 }
 
 size_t gemm_tc_workspace_bytes(int M, int n_total, int K, int epi) {
   // Upper bound over segmentations of n_total into up to three parts.
-  const int base = epi == kEpiSwiglu ? (n_total + 63) / 64 : (n_total + tc::BM - 1) / tc::BM;
+  const bool sw = epi == kEpiSwiglu;
+  const int base = (n_total + tc::BM - 1) / tc::BM;
   size_t best = 0;
-  for (int extra = 0; extra <= (epi == kEpiSwiglu ? 0 : 2); ++extra) {
-    const size_t b = tc::plan_ws_bytes(tc::make_plan(M, base + extra, K));
+  for (int extra = 0; extra <= (sw ? 0 : 2); ++extra) {
+    const size_t b = tc::plan_ws_bytes(tc::make_plan(M, base + extra, K, sw), sw);
     if (b > best) best = b;
   }
   return best;
@@ -556,14 +622,15 @@ int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int n
   B2_CHECK_ARG(nseg >= 1 && nseg <= tc::kMaxSegs, "gemm_tc: bad segment count");
   B2_CHECK_ARG(gemm_tc_supported(x, ldx, K, segs, nseg),
                "gemm_tc: needs K %% 8 == 0, 16-byte aligned rows (K=%d ldx=%lld)", K, (long long)ldx);
+  const bool sw = epi == kEpiSwiglu;
   tc::Params p{};
   int starts[tc::kMaxSegs + 1] = {0, 0, 0, 0};
   const int n_tiles = tc_tiles(segs, nseg, epi, starts);
-  const tc::Plan pl = tc::make_plan(M, n_tiles, K);
-  B2_CHECK_ARG(pl.m_tiles <= 65535, "gemm_tc: M=%d too large", M);
-  const size_t need = tc::plan_ws_bytes(pl);
+  const tc::Plan pl = tc::make_plan(M, n_tiles, K, sw);
+  const size_t need = tc::plan_ws_bytes(pl, sw);
   if (need > 0) {
     B2_CHECK_ARG(ws && ws_bytes >= need, "gemm_tc: workspace of %zu bytes needed, %zu given", need, ws_bytes);
+    B2_CHECK_ARG((size_t)pl.n_tiles * pl.m_tiles <= tc::kCounterSlots, "gemm_tc: too many tiles for split-K");
   }
   p.M = M;
   p.nkb = pl.nkb;
@@ -571,7 +638,7 @@ int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int n
   p.splits = pl.splits;
   p.n_tiles = n_tiles;
   p.m_tiles = pl.m_tiles;
-  p.nseg = epi == kEpiSwiglu ? 1 : nseg;
+  p.nseg = sw ? 1 : nseg;
   for (int i = 0; i <= tc::kMaxSegs; ++i) p.seg_tile_start[i] = starts[i];
   for (int i = 0; i < nseg; ++i) {
     p.seg_n[i] = segs[i].n;
@@ -583,29 +650,20 @@ int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int n
   p.ldy = ldy;
   p.y_dtype = y_dtype;
   if (need > 0) {
-    B2_CHECK_ARG((size_t)pl.n_tiles * pl.m_tiles <= tc::kCounterSlots, "gemm_tc: too many tiles for split-K");
     p.counters = reinterpret_cast<int*>(ws);
     p.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + tc::kCounterBytes);
   }
   p.status = status;
 
   CUtensorMap mx, mw[3];
-  const uint32_t wrows = epi == kEpiSwiglu ? 64 : tc::BM;
   int rc = tc::make_map(&mx, x, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 2, (uint32_t)pl.BN);
   if (rc) return rc;
   for (int i = 0; i < 3; ++i) {
     const GemmSeg& sg = segs[i < nseg ? i : 0];
-    rc = tc::make_map(&mw[i], sg.w, (uint64_t)K, (uint64_t)sg.n, (uint64_t)K * 2, wrows);
+    rc = tc::make_map(&mw[i], sg.w, (uint64_t)K, (uint64_t)sg.n, (uint64_t)K * 2, tc::BM);
     if (rc) return rc;
   }
-  dim3 grid(n_tiles, pl.m_tiles, pl.splits);
-  switch (pl.BN) {
-    case 16: return tc::launch<16>(mx, mw[0], mw[1], mw[2], p, grid, s);
-    case 32: return tc::launch<32>(mx, mw[0], mw[1], mw[2], p, grid, s);
-    case 64: return tc::launch<64>(mx, mw[0], mw[1], mw[2], p, grid, s);
-    case 128: return tc::launch<128>(mx, mw[0], mw[1], mw[2], p, grid, s);
-    default: return tc::launch<256>(mx, mw[0], mw[1], mw[2], p, grid, s);
-  }
+  return sw ? tc::launch_bn<true>(pl.BN, mx, mw, p, pl.ctas, s) : tc::launch_bn<false>(pl.BN, mx, mw, p, pl.ctas, s);
 }
 
 }  // namespace b2
