@@ -481,6 +481,205 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Split-K with the reduction in distributed shared memory.  One thread-block cluster per
+// output tile, one CTA per K split (cluster rank = split).  After its mainloop each CTA
+// copies its float32 partial tile from TMEM into its (now idle) pipeline shared memory;
+// after a cluster barrier, CTA k sums column slice k of every CTA's partial through
+// DSMEM (mapa + ld.shared::cluster) and stores that slice; a second cluster barrier keeps
+// every CTA resident until its partial has been read.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t local_smem, uint32_t cta) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem), "r"(cta));
+  return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+  return v;
+}
+
+template <int BN, bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_cluster_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW0,
+                           const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmW2,
+                           const Params p) {
+  using C = Cfg<BN, SWIGLU>;
+  constexpr int STAGES = C::STAGES;
+  constexpr int PARTS = SWIGLU ? 2 : 1;
+  static_assert((size_t)PARTS * BN * BM * 4 <= (size_t)STAGES * C::STAGE_BYTES, "partial tile must fit the ring");
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t acc_full;
+  __shared__ uint32_t tmem_slot;
+
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = (int)cluster_rank();
+  const int tile = blockIdx.x / p.splits;
+  const int mt = blockIdx.y;
+  int seg = 0;
+  if (p.nseg > 1 && tile >= p.seg_tile_start[1]) seg = 1;
+  if (p.nseg > 2 && tile >= p.seg_tile_start[2]) seg = 2;
+  const int local_tile = tile - (seg == 0 ? p.seg_tile_start[0] : seg == 1 ? p.seg_tile_start[1] : p.seg_tile_start[2]);
+  const int seg_n = seg == 0 ? p.seg_n[0] : seg == 1 ? p.seg_n[1] : p.seg_n[2];
+  const int seg_col = seg == 0 ? p.seg_col[0] : seg == 1 ? p.seg_col[1] : p.seg_col[2];
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(p.nkb, kb0 + p.kb_per_split);
+  const int m0 = mt * BN;
+  const int ncols = min(BN, p.M - m0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&acc_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int it = 0;
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int st = it % STAGES;
+        const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+        if (!mbar_wait(&empty_bar[st], ph ^ 1u)) {
+          raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+          break;
+        }
+        uint8_t* sa = smem + (size_t)st * C::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full_bar[st], C::STAGE_BYTES);
+        const int kx = kb * BK;
+        if (SWIGLU) {
+          tma_load_2d(sa, &tmW0, &full_bar[st], kx, local_tile * BM, pol_w);
+          tma_load_2d(sa + BM * BK * 2, &tmW1, &full_bar[st], kx, local_tile * BM, pol_w);
+        } else if (seg == 0) {
+          tma_load_2d(sa, &tmW0, &full_bar[st], kx, local_tile * BM, pol_w);
+        } else if (seg == 1) {
+          tma_load_2d(sa, &tmW1, &full_bar[st], kx, local_tile * BM, pol_w);
+        } else {
+          tma_load_2d(sa, &tmW2, &full_bar[st], kx, local_tile * BM, pol_w);
+        }
+        tma_load_2d(sa + C::A_BYTES, &tmX, &full_bar[st], kx, m0, pol_x);
+      }
+      for (int st = 0; st < STAGES && st < it; ++st) {
+        const int last_i = st + ((it - 1 - st) / STAGES) * STAGES;
+        mbar_wait(&full_bar[st], (uint32_t)(last_i / STAGES) & 1u, 100000000ull);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc_bf16(BM, BN);
+      int it = 0;
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int st = it % STAGES;
+        const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+        if (!mbar_wait(&full_bar[st], ph)) {
+          raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + (size_t)st * C::STAGE_BYTES);
+        const uint64_t adesc = smem_desc_sw128(a_addr);
+        const uint64_t bdesc = smem_desc_sw128(a_addr + C::A_BYTES);
+        const uint32_t first = kb == kb0 ? 1u : 0u;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          umma_bf16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
+        if (SWIGLU) {
+          const uint64_t udesc = smem_desc_sw128(a_addr + BM * BK * 2);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16(tmem + BN, udesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
+        }
+        umma_commit(&empty_bar[st]);
+      }
+      umma_commit(&acc_full);
+    }
+    __syncwarp();
+  }
+
+  // Stage the partial tile [part][column][128 rows] in this CTA's shared memory.
+  float* stage = reinterpret_cast<float*>(smem);
+  if (warp >= 2) {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t acc = tmem + ((uint32_t)(quarter * 32) << 16);
+    const bool done = mbar_wait(&acc_full, 0);
+    if (!done && lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+    tc_fence_after();
+    for (int c0 = 0; c0 < ncols; c0 += 16) {
+#pragma unroll
+      for (int part = 0; part < PARTS; ++part) {
+        float v[16];
+        tmem_ld16(acc + part * BN + c0, v);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) stage[(part * BN + c0 + e) * BM + r] = done ? v[e] : 0.f;
+      }
+    }
+  }
+  cluster_sync_all();
+
+  // Reduce this CTA's column slice over every split's partial, then store it.
+  const int per = (ncols + p.splits - 1) / p.splits;
+  const int c_lo = split * per, c_hi = min(ncols, c_lo + per);
+  const int r4 = lane * 4;
+  const int nb = local_tile * BM + r4;
+  const uint32_t stage_u32 = smem_u32(stage);
+  for (int c = c_lo + warp; c < c_hi; c += kThreads / 32) {
+    float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), u4 = g4;
+    for (int q = 0; q < p.splits; ++q) {
+      const uint32_t base = map_to_cta(stage_u32, (uint32_t)q);
+      const float4 a = ld_dsmem_f4(base + (uint32_t)((c * BM + r4) * 4));
+      g4.x += a.x; g4.y += a.y; g4.z += a.z; g4.w += a.w;
+      if (SWIGLU) {
+        const float4 b = ld_dsmem_f4(base + (uint32_t)(((BN + c) * BM + r4) * 4));
+        u4.x += b.x; u4.y += b.y; u4.z += b.z; u4.w += b.w;
+      }
+    }
+    const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+    const float uv[4] = {u4.x, u4.y, u4.z, u4.w};
+    const int64_t rowoff = (int64_t)(m0 + c) * p.ldy + seg_col;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (nb + e >= seg_n) continue;
+      const float bv = (!SWIGLU && p.bias) ? p.bias[seg_col + nb + e] : 0.f;
+      const float val = SWIGLU ? silu_f32(gv[e]) * uv[e] : gv[e] + bv;
+      st_dyn(p.y, p.y_dtype, rowoff + nb + e, val);
+    }
+  }
+  cluster_sync_all();  // every peer has finished reading this CTA's partial
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -510,13 +709,21 @@ static int make_map(CUtensorMap* m, const void* ptr, uint64_t k, uint64_t rows, 
   return B2_OK;
 }
 
+// The DSMEM split-K path stages the float32 partial tile in the idle pipeline ring.
+#define BN_FITS_CLUSTER(bn, swiglu) ((bn) <= 128)
+
 struct Plan {
   int BN, m_tiles, n_tiles, nkb, splits, kbps, ctas;
+  bool cluster;  // split-K reduced through DSMEM (one cluster per tile) instead of the workspace
 };
 
-// Split-K choice for the persistent kernel: each CTA streams ceil(units / SMs) units of
-// kbps k-blocks; split-K adds one float32 partial tile write per unit and a reduction
-// of all partials by the tile's last split.  Costs are bytes through one SM.
+// Launch plan.  Measured on B200 over the decode shapes (M = 1..128 tokens; q|k|v,
+// o_proj, gate|up, down of the 8B shape): when the output has at least half as many
+// 128-row tiles as there are SMs, the persistent kernel without split-K streams best;
+// otherwise split K over a thread-block cluster of s CTAs per tile, reduced in DSMEM,
+// with the largest s in {8, 4, 2} whose CTAs fit in one wave (clusters of 3, 5 or 6
+// schedule measurably worse).  The persistent split-K path with a global workspace
+// remains for token tiles too wide for the DSMEM staging (BN = 256).
 static Plan make_plan(int M, int n_tiles, int K, bool swiglu) {
   Plan pl{};
   pl.BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
@@ -525,22 +732,23 @@ static Plan make_plan(int M, int n_tiles, int K, bool swiglu) {
   pl.nkb = (K + BK - 1) / BK;
   const int sms = sm_count();
   const long tiles = (long)n_tiles * pl.m_tiles;
-  const long stage = (long)((swiglu ? 2 : 1) * BM + pl.BN) * BK * 2;
-  const long partial = (long)(swiglu ? 2 : 1) * BM * pl.BN * 4;
-  long best_cost = -1;
-  for (int s = 1; s <= 16 && s <= pl.nkb; ++s) {
-    const int kbps = (pl.nkb + s - 1) / s;
-    const int s_eff = (pl.nkb + kbps - 1) / kbps;
-    const long per_cta = (tiles * s_eff + sms - 1) / sms;
-    const long cost = per_cta * (kbps * stage + (s_eff > 1 ? partial : 0)) + (s_eff > 1 ? s_eff * partial : 0);
-    if (best_cost < 0 || cost < best_cost) {
-      best_cost = cost;
+  pl.splits = 1;
+  pl.kbps = pl.nkb;
+  pl.cluster = false;
+  if (2 * tiles < sms) {
+    for (int s : {8, 4, 2}) {
+      if (tiles * s > sms || s > pl.nkb) continue;
+      const int kbps = (pl.nkb + s - 1) / s;
+      const int s_eff = (pl.nkb + kbps - 1) / kbps;
+      if (s_eff < 2) continue;
       pl.splits = s_eff;
       pl.kbps = kbps;
+      pl.cluster = BN_FITS_CLUSTER(pl.BN, swiglu) && (s_eff == 2 || s_eff == 4 || s_eff == 8);
+      break;
     }
   }
   const long units = tiles * pl.splits;
-  pl.ctas = (int)(units < sms ? units : sms);
+  pl.ctas = pl.cluster ? (int)units : (int)(units < sms ? units : sms);
   return pl;
 }
 
@@ -550,7 +758,7 @@ constexpr size_t kCounterSlots = 65536;
 constexpr size_t kCounterBytes = kCounterSlots * sizeof(int);
 
 static size_t plan_ws_bytes(const Plan& pl, bool swiglu) {
-  if (pl.splits <= 1) return 0;
+  if (pl.splits <= 1 || pl.cluster) return 0;
   const size_t tiles = (size_t)pl.n_tiles * pl.m_tiles;
   return kCounterBytes + (size_t)pl.splits * tiles * (swiglu ? 2 : 1) * BM * pl.BN * sizeof(float);
 }
@@ -570,6 +778,45 @@ static int launch(const CUtensorMap& mx, const CUtensorMap& w0, const CUtensorMa
   gemm_tc_kernel<BN, SWIGLU><<<ctas, kThreads, C::SMEM, s>>>(mx, w0, w1, w2, p);
   B2_TRY_CUDA(cudaGetLastError());
   return B2_OK;
+}
+
+template <int BN, bool SWIGLU>
+static int launch_cluster(const CUtensorMap& mx, const CUtensorMap& w0, const CUtensorMap& w1,
+                          const CUtensorMap& w2, const Params& p, cudaStream_t s) {
+  using C = Cfg<BN, SWIGLU>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  B2_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    B2_TRY_CUDA(cudaFuncSetAttribute(gemm_tc_cluster_kernel<BN, SWIGLU>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+    attr_set[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.n_tiles * p.splits), (unsigned)p.m_tiles, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)p.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2_TRY_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_cluster_kernel<BN, SWIGLU>, mx, w0, w1, w2, p));
+  return B2_OK;
+}
+
+template <bool SWIGLU>
+static int launch_cluster_bn(int BN, const CUtensorMap& mx, const CUtensorMap* mw, const Params& p,
+                             cudaStream_t s) {
+  switch (BN) {
+    case 16: return launch_cluster<16, SWIGLU>(mx, mw[0], mw[1], mw[2], p, s);
+    case 32: return launch_cluster<32, SWIGLU>(mx, mw[0], mw[1], mw[2], p, s);
+    case 64: return launch_cluster<64, SWIGLU>(mx, mw[0], mw[1], mw[2], p, s);
+    default: return launch_cluster<128, SWIGLU>(mx, mw[0], mw[1], mw[2], p, s);
+  }
 }
 
 template <bool SWIGLU>
@@ -663,6 +910,8 @@ int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int n
     rc = tc::make_map(&mw[i], sg.w, (uint64_t)K, (uint64_t)sg.n, (uint64_t)K * 2, tc::BM);
     if (rc) return rc;
   }
+  if (pl.cluster)
+    return sw ? tc::launch_cluster_bn<true>(pl.BN, mx, mw, p, s) : tc::launch_cluster_bn<false>(pl.BN, mx, mw, p, s);
   return sw ? tc::launch_bn<true>(pl.BN, mx, mw, p, pl.ctas, s) : tc::launch_bn<false>(pl.BN, mx, mw, p, pl.ctas, s);
 }
 

@@ -48,6 +48,77 @@ __global__ void rmsnorm_kernel(const void* x, int x_dtype, const void* res, int 
   }
 }
 
+// Vectorised RMSNorm for rows of dim % 8 == 0 and dim <= 8 * 4 * blockDim: each thread
+// keeps its (up to 4) 8-element slices of h in registers, so the row is read once.
+template <typename TX>
+__device__ __forceinline__ void ld8(const void* p, int dtype, size_t i, float (&v)[8]) {
+  if (dtype == B2_BF16) {
+    load16_f32<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(p) + i, v);
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+__device__ __forceinline__ void st8(void* p, int dtype, size_t i, const float (&v)[8]) {
+  if (dtype == B2_BF16) {
+    uint4 o;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+      w[k] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p) + i) = o;
+  } else {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + i) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + i + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+}
+
+__global__ void rmsnorm_vec_kernel(const void* x, int x_dtype, const void* res, int res_dtype, void* h_out,
+                                   int h_dtype, const float* __restrict__ w, float eps, void* y, int y_dtype,
+                                   int dim) {
+  __shared__ float red[32];
+  const size_t base = (size_t)blockIdx.x * dim;
+  const int nv = dim / 8;
+  float v[4][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int j = threadIdx.x + it * blockDim.x;
+    if (j < nv) {
+      ld8<float>(x, x_dtype, base + (size_t)j * 8, v[it]);
+      if (res) {
+        float r[8];
+        ld8<float>(res, res_dtype, base + (size_t)j * 8, r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[it][e] += r[e];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[it][e] * v[it][e];
+    }
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / (float)dim + eps);
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int j = threadIdx.x + it * blockDim.x;
+    if (j < nv) {
+      if (h_out) st8(h_out, h_dtype, base + (size_t)j * 8, v[it]);
+      if (y) {
+        float o[8];
+        const float4 wa = *reinterpret_cast<const float4*>(w + j * 8);
+        const float4 wb = *reinterpret_cast<const float4*>(w + j * 8 + 4);
+        const float ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = v[it][e] * inv * ww[e];
+        st8(y, y_dtype, base + (size_t)j * 8, o);
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- argmax
 // First index of the row maximum, like torch.argmax (execution_engine.py:103,133).
 __global__ void argmax_kernel(const float* __restrict__ logits, int64_t ld, int cols,
@@ -57,12 +128,33 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int64_t ld, int 
   const float* row = logits + (size_t)blockIdx.x * ld;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-    const float v = row[c];
+  auto take = [&](float v, int c) {
     if (v > best || (v == best && c < bi) || (v != v && best == best)) {  // NaN wins, like torch
       best = v;
       bi = c;
     }
+  };
+  if ((((uintptr_t)row) & 15) == 0) {
+    const int n4 = cols / 4;
+    const float4* row4 = reinterpret_cast<const float4*>(row);
+    int c4 = threadIdx.x;
+    for (; c4 + 3 * (int)blockDim.x < n4; c4 += 4 * blockDim.x) {  // four 16-byte loads in flight
+      float4 a[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = __ldg(row4 + c4 + u * blockDim.x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = 4 * (c4 + u * blockDim.x);
+        take(a[u].x, c); take(a[u].y, c + 1); take(a[u].z, c + 2); take(a[u].w, c + 3);
+      }
+    }
+    for (; c4 < n4; c4 += blockDim.x) {
+      const float4 a = __ldg(row4 + c4);
+      take(a.x, 4 * c4); take(a.y, 4 * c4 + 1); take(a.z, 4 * c4 + 2); take(a.w, 4 * c4 + 3);
+    }
+    for (int c = 4 * n4 + threadIdx.x; c < cols; c += blockDim.x) take(row[c], c);
+  } else {
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) take(row[c], c);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -121,6 +213,17 @@ int b2_rmsnorm(const void* x, int x_dtype, const void* residual, int residual_dt
   B2_CHECK_ARG(dim <= 12288, "b2_rmsnorm: dim %d exceeds 12288", dim);
   if (rows == 0) return B2_OK;
   B2_CHECK_ARG(x && (y ? weight != nullptr : h_out != nullptr), "b2_rmsnorm: null pointer");
+  auto al16 = [](const void* q) { return q == nullptr || ((uintptr_t)q % 16) == 0; };
+  if (dim % 8 == 0 && dim <= 8 * 4 * 256 && al16(x) && al16(residual) && al16(h_out) && al16(y) && al16(weight)) {
+    const int nv = dim / 8;
+    int threads = 32;
+    while (threads < 256 && threads * 4 < nv) threads *= 2;
+    while (threads < nv && threads < 256 && nv / threads > 1) threads *= 2;
+    b2::rmsnorm_vec_kernel<<<rows, threads, 0, stream>>>(x, x_dtype, residual, residual_dtype, h_out, h_dtype,
+                                                          weight, eps, y, y_dtype, dim);
+    B2_TRY_CUDA(cudaGetLastError());
+    return B2_OK;
+  }
   const size_t smem = (size_t)dim * sizeof(float);
   if (smem > 48 * 1024) {
     B2_TRY_CUDA(cudaFuncSetAttribute(b2::rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -137,7 +240,7 @@ int b2_argmax(const float* logits, int64_t ld, int rows, int cols, int64_t* out,
   B2_CHECK_ARG(rows >= 0 && cols > 0 && ld >= cols, "b2_argmax: bad sizes");
   if (rows == 0) return B2_OK;
   B2_CHECK_ARG(logits && out, "b2_argmax: null pointer");
-  b2::argmax_kernel<<<rows, 512, 0, stream>>>(logits, ld, cols, out);
+  b2::argmax_kernel<<<rows, 1024, 0, stream>>>(logits, ld, cols, out);
   B2_TRY_CUDA(cudaGetLastError());
   return B2_OK;
 }
