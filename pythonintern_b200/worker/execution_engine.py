@@ -26,12 +26,14 @@ from pythonintern_b200.model.kv_cache import KVCacheManager
 from pythonintern_b200.model.llama import DistributedLLaMAModel
 from pythonintern_b200.model.metadata import PinnedStager, build_metadata
 from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
+from pythonintern_b200.worker.graphs import DecodeGraphCache
 from pythonintern_b200.worker.messages import SampledToken, StepResponse
 
 
 class WorkerExecutionEngine:
     def __init__(self, model_config: ModelConfig, shard_config: ShardConfig, kv_config: KVCacheConfig,
-                 communicator: Optional[DistributedCommunicator] = None, device="cuda"):
+                 communicator: Optional[DistributedCommunicator] = None, device="cuda",
+                 use_cuda_graphs: bool = True):
         self.model_config = model_config
         self.shard_config = shard_config
         self.kv_config = kv_config
@@ -47,6 +49,8 @@ class WorkerExecutionEngine:
         self.model = DistributedLLaMAModel(config=model_config, rank=shard_config.rank,
                                            world_size=shard_config.world_size, communicator=communicator, device=dev)
         self.stager = PinnedStager(dev)
+        self.use_cuda_graphs = use_cuda_graphs
+        self.graphs = DecodeGraphCache(self.model, self.kv_manager.pool, model_config.masked_decode_padding)
         self.total_steps_executed = 0
         self.total_latency_ms = 0.0
         self.last_h2d_bytes = 0
@@ -84,12 +88,22 @@ class WorkerExecutionEngine:
                 tok_ids = np.asarray([[s.current_token_id] for s in decode_slots], dtype=np.int64)
                 pos = np.asarray([[s.current_len - 1] for s in decode_slots], dtype=np.int64)
                 tables = [list(s.block_table) for s in decode_slots]
-                md = build_metadata(pos, tables, False, self.device,
-                                    masked_padding=self.model_config.masked_decode_padding,
-                                    stager=self.stager, extra=tok_ids)
-                h2d += self.stager.last_bytes
-                logits = self.model(md.extra, None, pool, tables, False, step_id, True, metadata=md)
-                t, tl = self._sample(logits)
+                if self.use_cuda_graphs:
+                    # One graph replay per step (worker/graphs.py); captured on first use.
+                    g, new = self.graphs.get(len(decode_slots), max(len(t) for t in tables))
+                    g.upload_host(tok_ids.reshape(-1), pos.reshape(-1), tables)
+                    h2d += g.nbytes
+                    if new:
+                        g.capture()
+                    t, logits = g.replay()
+                    tl = logits[:, :10]
+                else:
+                    md = build_metadata(pos, tables, False, self.device,
+                                        masked_padding=self.model_config.masked_decode_padding,
+                                        stager=self.stager, extra=tok_ids)
+                    h2d += self.stager.last_bytes
+                    logits = self.model(md.extra, None, pool, tables, False, step_id, True, metadata=md)
+                    t, tl = self._sample(logits)
                 toks.append(t)
                 tops.append(tl)
                 ids.extend(s.seq_id for s in decode_slots)
