@@ -308,4 +308,6 @@ def test_decode_graph_replay_matches_eager():
         outs.append(hist)
     for (ta, la), (tb, lb) in zip(*outs):
         assert ta == tb
-        assert np.array_equal(np.asarray(la), np.asarray(lb))
+        # the graph sizes its attention split count for the bucket's width, so the split
+        # merge order (not the math) may differ from the eager call
+        np.testing.assert_allclose(np.asarray(la), np.asarray(lb), rtol=1e-5, atol=1e-5)
