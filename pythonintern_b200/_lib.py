@@ -66,6 +66,11 @@ _SIGS = {
     "b2_allreduce_sum": (_c_int, [_c_void_p, _c_int, _c_size, _c_int, _c_void_p, _c_i64, _c_void_p, _c_void_p]),
     "b2_allreduce_rmsnorm": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
                                       _c_void_p, _c_float, _c_void_p, _c_int, _c_i64, _c_void_p, _c_void_p]),
+    "b2_row_parallel_linear": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_i64, _c_int, _c_int, _c_void_p,
+                                        _c_int, _c_int, _c_void_p, _c_size, _c_void_p, _c_void_p]),
+    "b2_allreduce_rmsnorm_sharded": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_void_p,
+                                              _c_void_p, _c_float, _c_i64, _c_void_p, _c_void_p]),
+    "b2_comm_xn_buffer": (_c_int, [_c_void_p, _c_int, ctypes.POINTER(_c_void_p)]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -108,7 +113,8 @@ def last_error() -> str:
 # checked through ``check``); bench.py reads it to report its launch count.
 launch_count = 0
 _LAUNCHING = {"b2_embedding", "b2_rmsnorm", "b2_linear", "b2_linear_qkv", "b2_linear_swiglu",
-              "b2_rope_kv_write", "b2_paged_attention", "b2_argmax", "b2_allreduce_sum", "b2_allreduce_rmsnorm"}
+              "b2_rope_kv_write", "b2_paged_attention", "b2_argmax", "b2_allreduce_sum", "b2_allreduce_rmsnorm",
+              "b2_row_parallel_linear", "b2_allreduce_rmsnorm_sharded", "b2_paged_attention_noalloc"}
 
 
 def check(rc: int, what: str = ""):

@@ -25,6 +25,7 @@
 #include <new>
 
 #include "common.cuh"
+#include "gemm.cuh"
 
 namespace b2 {
 
@@ -32,8 +33,9 @@ constexpr int kMaxRanks = 8;
 constexpr int kMaxCtas = 128;
 
 struct CommView {
-  void* data[2][kMaxRanks];     // every rank's data buffers (own included)
-  uint32_t* flags[kMaxRanks];   // every rank's flag array [kMaxRanks][kMaxCtas]
+  void* data[2][kMaxRanks];     // every rank's data (receive) buffers (own included)
+  void* xn[2][kMaxRanks];       // every rank's all-gather buffers of normalised rows
+  uint32_t* flags[kMaxRanks];   // every rank's flag array [2 phases][kMaxRanks][kMaxCtas]
   uint32_t* ctrl;               // own {epoch, done}
   int rank, world;
 };
@@ -43,7 +45,8 @@ struct CommView {
 struct b2_comm {
   int rank, world, device;
   size_t max_bytes, data_bytes;
-  size_t off_data[2], off_flags, off_ctrl, total;
+  size_t off_data[2], off_xn[2], off_flags, off_ctrl, off_table, total;
+  unsigned long long* scatter_table;  // device: [2 parities][kMaxRanks] peer data buffer addresses
   char* base;                       // own allocation
   char* peer_base[b2::kMaxRanks];   // mapped peers (own base at [rank])
   cudaIpcMemHandle_t handle;
@@ -62,18 +65,21 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-// Steps 1-2 of the protocol.  Returns false (and raises the status bit) on timeout.
-__device__ bool comm_barrier(const CommView& v, uint32_t epoch, int64_t timeout_ns, int32_t* status) {
+// Steps 1-2 of the protocol (flag set `phase`).  Returns false (and raises the status
+// bit) on timeout.
+__device__ bool comm_barrier(const CommView& v, uint32_t epoch, int64_t timeout_ns, int32_t* status,
+                             int phase = 0) {
   __shared__ int s_ok;
   const int cta = blockIdx.x;
+  const int pofs = phase * kMaxRanks * kMaxCtas;
   if (threadIdx.x == 0) s_ok = 1;
   __syncthreads();
   if (threadIdx.x < v.world) {
     __threadfence_system();
-    st_release_sys(v.flags[threadIdx.x] + v.rank * kMaxCtas + cta, epoch);
+    st_release_sys(v.flags[threadIdx.x] + pofs + v.rank * kMaxCtas + cta, epoch);
   }
   if (threadIdx.x < v.world) {
-    const uint32_t* f = v.flags[v.rank] + threadIdx.x * kMaxCtas + cta;
+    const uint32_t* f = v.flags[v.rank] + pofs + threadIdx.x * kMaxCtas + cta;
     const uint64_t t0 = globaltimer_ns();
     uint32_t it = 0;
     while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
@@ -120,6 +126,25 @@ __device__ __forceinline__ void load8<float>(const float* p, float (&o)[8]) {
   const float4 b = __ldcv(reinterpret_cast<const float4*>(p) + 1);
   o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
   o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T* dst, const float (&v)[8]);
+template <>
+__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* dst, const float (&v)[8]) {
+  uint4 o;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+    w[k] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+  *reinterpret_cast<uint4*>(dst) = o;
+}
+template <>
+__device__ __forceinline__ void store8<float>(float* dst, const float (&v)[8]) {
+  reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
 
 // out[i] = sum_r data_r[parity][i], 8 elements per thread step.
@@ -185,6 +210,69 @@ __global__ void allreduce_rmsnorm_kernel(CommView v, int parity, int rows, int d
   comm_finish(v);
 }
 
+// Second half of the row-parallel all-reduce with a row-sharded residual.  The partials
+// were pushed by the row-parallel GEMM of every rank into this rank's data buffer as
+// [src][R][dim] (R = rows per rank).  After barrier 0, each CTA takes owned rows
+// (global row = rank * R + lr): h = h_slice + sum over src (rank order), h_slice = h,
+// y = rmsnorm(h) * w, and pushes y into row `row` of EVERY rank's xn buffer.  Barrier 1
+// then guarantees that all rows of the xn buffer are in place on every rank.
+template <typename T>
+__global__ void allreduce_rmsnorm_sharded_kernel(CommView v, int parity, int rows, int R, int dim,
+                                                 float* h_slice, const float* __restrict__ w, float eps,
+                                                 int64_t timeout_ns, int32_t* status) {
+  __shared__ float red[32];
+  const uint32_t epoch = v.ctrl[0] + 1;
+  bool ok = comm_barrier(v, epoch, timeout_ns, status, 0);
+  const int nv = dim / 8;
+  if (ok) {
+    const T* recv = reinterpret_cast<const T*>(v.data[parity][v.rank]);
+    for (int lr = blockIdx.x; lr < R; lr += gridDim.x) {
+      const int row = v.rank * R + lr;
+      if (row >= rows) break;  // uniform across the CTA
+      float hv[4][8];
+      float ss = 0.f;
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int j = threadIdx.x + it * blockDim.x;
+        if (j >= nv) continue;
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int src = 0; src < v.world; ++src) {
+          float x[8];
+          load8<T>(recv + ((size_t)src * R + lr) * dim + j * 8, x);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += x[e];
+        }
+        float* hp = h_slice + (size_t)lr * dim + j * 8;
+        const float4 h0 = *reinterpret_cast<const float4*>(hp);
+        const float4 h1 = *reinterpret_cast<const float4*>(hp + 4);
+        const float hr[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          hv[it][e] = hr[e] + acc[e];
+          ss += hv[it][e] * hv[it][e];
+        }
+        *reinterpret_cast<float4*>(hp) = make_float4(hv[it][0], hv[it][1], hv[it][2], hv[it][3]);
+        *reinterpret_cast<float4*>(hp + 4) = make_float4(hv[it][4], hv[it][5], hv[it][6], hv[it][7]);
+      }
+      ss = block_sum(ss, red);
+      const float inv = rsqrtf(ss / (float)dim + eps);
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int j = threadIdx.x + it * blockDim.x;
+        if (j >= nv) continue;
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = hv[it][e] * inv * w[j * 8 + e];
+        for (int q = 0; q < v.world; ++q)  // all-gather by posted stores (own buffer included)
+          store8<T>(reinterpret_cast<T*>(v.xn[parity][q]) + (size_t)row * dim + j * 8, o);
+      }
+      __syncthreads();
+    }
+  }
+  if (ok) ok = comm_barrier(v, epoch, timeout_ns, status, 1);
+  comm_finish(v);
+}
+
 static CommView make_view(const b2_comm* c) {
   CommView v{};
   v.rank = c->rank;
@@ -192,6 +280,8 @@ static CommView make_view(const b2_comm* c) {
   for (int r = 0; r < c->world; ++r) {
     v.data[0][r] = c->peer_base[r] + c->off_data[0];
     v.data[1][r] = c->peer_base[r] + c->off_data[1];
+    v.xn[0][r] = c->peer_base[r] + c->off_xn[0];
+    v.xn[1][r] = c->peer_base[r] + c->off_xn[1];
     v.flags[r] = reinterpret_cast<uint32_t*>(c->peer_base[r] + c->off_flags);
   }
   v.ctrl = reinterpret_cast<uint32_t*>(c->base + c->off_ctrl);
@@ -199,6 +289,21 @@ static CommView make_view(const b2_comm* c) {
 }
 
 static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Fills the device table of every rank's data-buffer address (as seen from this rank).
+static int fill_scatter_table(b2_comm* c) {
+  unsigned long long t[2 * kMaxRanks] = {0};
+  for (int par = 0; par < 2; ++par)
+    for (int r = 0; r < c->world; ++r)
+      t[par * kMaxRanks + r] = (unsigned long long)(uintptr_t)(c->peer_base[r] + c->off_data[par]);
+  int dev = 0;
+  B2_TRY_CUDA(cudaGetDevice(&dev));
+  B2_TRY_CUDA(cudaSetDevice(c->device));
+  cudaError_t e = cudaMemcpy(c->scatter_table, t, sizeof(t), cudaMemcpyHostToDevice);
+  cudaSetDevice(dev);
+  if (e != cudaSuccess) return fail(B2_ECUDA, "scatter table upload: %s", cudaGetErrorString(e));
+  return B2_OK;
+}
 
 }  // namespace b2
 
@@ -220,16 +325,19 @@ int b2_comm_create(int rank, int world_size, size_t max_bytes, b2_comm** out) {
   c->data_bytes = b2::align_up(max_bytes, 4096);
   c->off_data[0] = 0;
   c->off_data[1] = c->data_bytes;
-  c->off_flags = 2 * c->data_bytes;
-  c->off_ctrl = c->off_flags + b2::align_up((size_t)b2::kMaxRanks * b2::kMaxCtas * sizeof(uint32_t), 256);
-  c->total = c->off_ctrl + 256;
+  c->off_xn[0] = 2 * c->data_bytes;
+  c->off_xn[1] = 3 * c->data_bytes;
+  c->off_flags = 4 * c->data_bytes;
+  c->off_ctrl = c->off_flags + b2::align_up((size_t)2 * b2::kMaxRanks * b2::kMaxCtas * sizeof(uint32_t), 256);
+  c->off_table = c->off_ctrl + 256;
+  c->total = c->off_table + 256;
   cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&c->base), c->total);
   if (e != cudaSuccess) {
     delete c;
     return b2::fail(B2_ECUDA, "b2_comm_create: cudaMalloc(%zu): %s", (size_t)0, cudaGetErrorString(e));
   }
   e = cudaMemset(c->base + c->off_flags, 0, c->total - c->off_flags);
-  if (e == cudaSuccess) e = cudaMemset(c->base, 0, 2 * c->data_bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->base, 0, 4 * c->data_bytes);
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&c->handle, c->base);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
@@ -239,8 +347,17 @@ int b2_comm_create(int rank, int world_size, size_t max_bytes, b2_comm** out) {
   }
   for (int r = 0; r < b2::kMaxRanks; ++r) c->peer_base[r] = nullptr;
   c->peer_base[rank] = c->base;
+  c->scatter_table = reinterpret_cast<unsigned long long*>(c->base + c->off_table);
   c->opened = world_size == 1;
   c->local_peers = false;
+  if (world_size == 1) {
+    const int rc = b2::fill_scatter_table(c);
+    if (rc) {
+      cudaFree(c->base);
+      delete c;
+      return rc;
+    }
+  }
   *out = c;
   return B2_OK;
 }
@@ -274,7 +391,7 @@ int b2_comm_open_peers(b2_comm* comm, const void* all_handles, size_t len) {
     comm->peer_base[r] = static_cast<char*>(p);
   }
   comm->opened = true;
-  return B2_OK;
+  return b2::fill_scatter_table(comm);
 }
 
 int b2_comm_open_local(b2_comm* const* comms, int n) {
@@ -312,6 +429,8 @@ int b2_comm_open_local(b2_comm* const* comms, int n) {
     for (int j = 0; j < n; ++j) comms[i]->peer_base[j] = comms[j]->base;
     comms[i]->opened = true;
     comms[i]->local_peers = true;
+    const int rc = b2::fill_scatter_table(comms[i]);
+    if (rc) return rc;
   }
   return B2_OK;
 }
@@ -319,6 +438,12 @@ int b2_comm_open_local(b2_comm* const* comms, int n) {
 int b2_comm_buffer(b2_comm* comm, int parity, void** ptr) {
   B2_CHECK_ARG(comm && ptr && (parity == 0 || parity == 1), "b2_comm_buffer: bad arguments");
   *ptr = comm->base + comm->off_data[parity];
+  return B2_OK;
+}
+
+int b2_comm_xn_buffer(b2_comm* comm, int parity, void** ptr) {
+  B2_CHECK_ARG(comm && ptr && (parity == 0 || parity == 1), "b2_comm_xn_buffer: bad arguments");
+  *ptr = comm->base + comm->off_xn[parity];
   return B2_OK;
 }
 
@@ -385,6 +510,54 @@ int b2_allreduce_rmsnorm(b2_comm* comm, int parity, int rows, int dim, int dtype
     b2::allreduce_rmsnorm_kernel<float><<<grid, threads, smem, stream>>>(
         v, parity, rows, dim, residual, h_out, norm_w, eps, y, y_dtype, timeout_ns, status);
   }
+  B2_TRY_CUDA(cudaGetLastError());
+  return B2_OK;
+}
+
+int b2_row_parallel_linear(b2_comm* comm, int parity, const void* x, int64_t ldx, int M, int K, const void* w,
+                           int N, int dtype, void* workspace, size_t workspace_bytes, int32_t* status,
+                           b2_stream_t stream) {
+  B2_CHECK_ARG(comm && comm->opened, "b2_row_parallel_linear: communicator not opened");
+  B2_CHECK_ARG(parity == 0 || parity == 1, "b2_row_parallel_linear: parity must be 0 or 1");
+  B2_CHECK_ARG(b2::valid_dtype(dtype), "b2_row_parallel_linear: bad dtype");
+  B2_CHECK_ARG(M >= 0 && K > 0 && N > 0 && ldx >= K, "b2_row_parallel_linear: bad sizes");
+  if (M == 0) return B2_OK;
+  B2_CHECK_ARG(x && w, "b2_row_parallel_linear: null pointer");
+  const int R = (M + comm->world - 1) / comm->world;
+  B2_CHECK_ARG((size_t)comm->world * R * N * b2::dtype_bytes(dtype) <= comm->max_bytes,
+               "b2_row_parallel_linear: %d x %d partial exceeds the communicator buffer", M, N);
+  b2::Scatter sc{comm->scatter_table + parity * b2::kMaxRanks, R, comm->rank, comm->world};
+  if (dtype == B2_F32) return b2::gemm_simt(x, ldx, M, K, w, nullptr, N, nullptr, nullptr, N, dtype, dtype, stream, &sc);
+  b2::GemmSeg seg{w, N, 0};
+  return b2::gemm_tc(x, ldx, M, K, &seg, 1, b2::kEpiStore, nullptr, nullptr, N, dtype, workspace, workspace_bytes,
+                     status, stream, &sc);
+}
+
+int b2_allreduce_rmsnorm_sharded(b2_comm* comm, int parity, int rows, int dim, int dtype, float* h_slice,
+                                 const float* norm_w, float eps, int64_t timeout_ns, int32_t* status,
+                                 b2_stream_t stream) {
+  B2_CHECK_ARG(comm && comm->opened, "b2_allreduce_rmsnorm_sharded: communicator not opened");
+  B2_CHECK_ARG(parity == 0 || parity == 1, "b2_allreduce_rmsnorm_sharded: parity must be 0 or 1");
+  B2_CHECK_ARG(b2::valid_dtype(dtype), "b2_allreduce_rmsnorm_sharded: bad dtype");
+  B2_CHECK_ARG(rows >= 0 && dim > 0 && dim % 8 == 0 && dim <= 8 * 4 * 512,
+               "b2_allreduce_rmsnorm_sharded: bad dim %d", dim);
+  if (rows == 0) return B2_OK;
+  const int R = (rows + comm->world - 1) / comm->world;
+  B2_CHECK_ARG((size_t)comm->world * R * dim * b2::dtype_bytes(dtype) <= comm->max_bytes,
+               "b2_allreduce_rmsnorm_sharded: payload exceeds the buffer");
+  B2_CHECK_ARG(norm_w && (h_slice || comm->rank * R >= rows), "b2_allreduce_rmsnorm_sharded: null pointer");
+  B2_CHECK_ARG(((uintptr_t)h_slice % 16) == 0 && ((uintptr_t)norm_w % 16) == 0,
+               "b2_allreduce_rmsnorm_sharded: h_slice and norm_w must be 16-byte aligned");
+  const b2::CommView v = b2::make_view(comm);
+  const int grid = R < b2::kMaxCtas ? R : b2::kMaxCtas;
+  int threads = 64;
+  while (threads < 512 && threads * 4 < dim / 8) threads *= 2;
+  if (dtype == B2_BF16)
+    b2::allreduce_rmsnorm_sharded_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
+        v, parity, rows, R, dim, h_slice, norm_w, eps, timeout_ns, status);
+  else
+    b2::allreduce_rmsnorm_sharded_kernel<float><<<grid, threads, 0, stream>>>(
+        v, parity, rows, R, dim, h_slice, norm_w, eps, timeout_ns, status);
   B2_TRY_CUDA(cudaGetLastError());
   return B2_OK;
 }

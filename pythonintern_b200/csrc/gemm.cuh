@@ -18,15 +18,36 @@ struct GemmSeg {
   int col_off;
 };
 
+// Reduce-scatter destination of a row-parallel GEMM: output row m goes to rank
+// o = m / rows_per_rank, at row (src * rows_per_rank + m % rows_per_rank) of the buffer
+// whose device address is table[o] (peer memory for o != src).  world == 0: plain output.
+struct Scatter {
+  const unsigned long long* table;
+  int rows_per_rank, src, world;
+};
+
 int gemm_simt(const void* x, int64_t ldx, int M, int K, const void* w0, const void* w1, int N,
-              const float* bias, void* y, int64_t ldy, int dtype, int y_dtype, cudaStream_t s);
+              const float* bias, void* y, int64_t ldy, int dtype, int y_dtype, cudaStream_t s,
+              const Scatter* sc = nullptr);
+
+// Address of output element (m, col) for a plain or scattered destination.
+__device__ __forceinline__ void* out_base(void* y, int y_dtype, int64_t ldy, const unsigned long long* table,
+                                          int R, int src, int world, int64_t m, int64_t col, int64_t* idx) {
+  if (world > 0) {
+    const int o = (int)(m / R);
+    *idx = ((int64_t)src * R + (m - (int64_t)o * R)) * ldy + col;
+    return reinterpret_cast<void*>(table[o]);
+  }
+  *idx = m * ldy + col;
+  return y;
+}
 
 // bf16 tcgen05 GEMM. For kEpiStore: nseg segments (1..3) concatenated along N.
 // For kEpiSwiglu: segs[0] = gate, segs[1] = up, both with n = N.
 size_t gemm_tc_workspace_bytes(int M, int n_total, int K, int epi);
 int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int nseg, int epi,
             const float* bias, void* y, int64_t ldy, int y_dtype, void* ws, size_t ws_bytes,
-            int32_t* status, cudaStream_t s);
+            int32_t* status, cudaStream_t s, const Scatter* sc = nullptr);
 // Returns true when the tensor-core kernel supports the shape (K % 8 == 0, 16-byte aligned rows).
 bool gemm_tc_supported(const void* x, int64_t ldx, int K, const GemmSeg* segs, int nseg);
 

@@ -19,7 +19,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
                                                         const T* __restrict__ W1, int M, int N,
                                                         int K, const float* __restrict__ bias,
                                                         void* __restrict__ Y, int64_t ldy,
-                                                        int y_dtype) {
+                                                        int y_dtype, Scatter sc) {
   __shared__ float As[SBK][SBM + 4];
   __shared__ float Ws[SBK][SBN + 4];
   __shared__ float Us[SWIGLU ? SBK : 1][SWIGLU ? SBN + 4 : 1];
@@ -77,26 +77,31 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
       } else {
         if (bias) v += bias[n];
       }
-      st_dyn(Y, y_dtype, (int64_t)m * ldy + n, v);
+      int64_t idx;
+      void* base = out_base(Y, y_dtype, ldy, sc.table, sc.rows_per_rank, sc.src, sc.world, m, n, &idx);
+      st_dyn(base, y_dtype, idx, v);
     }
   }
+  if (sc.world > 0) __threadfence_system();
 }
 
 int gemm_simt(const void* x, int64_t ldx, int M, int K, const void* w0, const void* w1, int N,
-              const float* bias, void* y, int64_t ldy, int dtype, int y_dtype, cudaStream_t s) {
+              const float* bias, void* y, int64_t ldy, int dtype, int y_dtype, cudaStream_t s,
+              const Scatter* scp) {
+  const Scatter sc = scp ? *scp : Scatter{nullptr, 1, 0, 0};
   dim3 grid((N + SBN - 1) / SBN, (M + SBM - 1) / SBM);
   B2_CHECK_ARG(grid.y <= 65535, "gemm: M=%d too large", M);
   if (dtype == B2_BF16) {
     using T = __nv_bfloat16;
     if (w1)
-      gemm_simt_kernel<T, true><<<grid, 256, 0, s>>>((const T*)x, ldx, (const T*)w0, (const T*)w1, M, N, K, bias, y, ldy, y_dtype);
+      gemm_simt_kernel<T, true><<<grid, 256, 0, s>>>((const T*)x, ldx, (const T*)w0, (const T*)w1, M, N, K, bias, y, ldy, y_dtype, sc);
     else
-      gemm_simt_kernel<T, false><<<grid, 256, 0, s>>>((const T*)x, ldx, (const T*)w0, nullptr, M, N, K, bias, y, ldy, y_dtype);
+      gemm_simt_kernel<T, false><<<grid, 256, 0, s>>>((const T*)x, ldx, (const T*)w0, nullptr, M, N, K, bias, y, ldy, y_dtype, sc);
   } else {
     if (w1)
-      gemm_simt_kernel<float, true><<<grid, 256, 0, s>>>((const float*)x, ldx, (const float*)w0, (const float*)w1, M, N, K, bias, y, ldy, y_dtype);
+      gemm_simt_kernel<float, true><<<grid, 256, 0, s>>>((const float*)x, ldx, (const float*)w0, (const float*)w1, M, N, K, bias, y, ldy, y_dtype, sc);
     else
-      gemm_simt_kernel<float, false><<<grid, 256, 0, s>>>((const float*)x, ldx, (const float*)w0, nullptr, M, N, K, bias, y, ldy, y_dtype);
+      gemm_simt_kernel<float, false><<<grid, 256, 0, s>>>((const float*)x, ldx, (const float*)w0, nullptr, M, N, K, bias, y, ldy, y_dtype, sc);
   }
   B2_TRY_CUDA(cudaGetLastError());
   return B2_OK;

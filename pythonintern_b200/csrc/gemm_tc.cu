@@ -48,7 +48,15 @@ struct Params {
   float* ws;
   int* counters;
   int32_t* status;
+  const unsigned long long* sc_table;  // reduce-scatter destinations (sc_world > 0)
+  int sc_R, sc_src, sc_world;
 };
+
+__device__ __forceinline__ void store_out(const Params& p, int64_t m, int64_t col, float v) {
+  int64_t idx;
+  void* base = out_base(p.y, p.y_dtype, p.ldy, p.sc_table, p.sc_R, p.sc_src, p.sc_world, m, col, &idx);
+  st_dyn(base, p.y_dtype, idx, v);
+}
 
 // ------------------------------------------------------------------ PTX wrappers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -401,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (nok) {
 #pragma unroll
             for (int e = 0; e < 16; ++e)
-              if (c0 + e < ncols) st_dyn(p.y, p.y_dtype, (int64_t)(m0 + c0 + e) * p.ldy + col, v[e] + bv);
+              if (c0 + e < ncols) store_out(p, m0 + c0 + e, col, v[e] + bv);
           }
         }
         tc_fence_before();
@@ -458,12 +466,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
             const float uv[4] = {u4.x, u4.y, u4.z, u4.w};
-            const int64_t rowoff = (int64_t)(m0 + c) * p.ldy + seg_col;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               if (nb + e >= seg_n) continue;
               const float val = SWIGLU ? silu_f32(gv[e]) * uv[e] : gv[e] + bv[e];
-              st_dyn(p.y, p.y_dtype, rowoff + nb + e, val);
+              store_out(p, m0 + c, seg_col + nb + e, val);
             }
           }
         }
@@ -473,6 +480,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ---------------- teardown
+  // Scattered rows were stored into peer memory: make them visible system-wide before the
+  // CTA retires, so the consumer's flag barrier (after this kernel) orders them.
+  if (p.sc_world > 0) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -661,15 +671,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
     const float uv[4] = {u4.x, u4.y, u4.z, u4.w};
-    const int64_t rowoff = (int64_t)(m0 + c) * p.ldy + seg_col;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       if (nb + e >= seg_n) continue;
       const float bv = (!SWIGLU && p.bias) ? p.bias[seg_col + nb + e] : 0.f;
       const float val = SWIGLU ? silu_f32(gv[e]) * uv[e] : gv[e] + bv;
-      st_dyn(p.y, p.y_dtype, rowoff + nb + e, val);
+      store_out(p, m0 + c, seg_col + nb + e, val);
     }
   }
+  if (p.sc_world > 0) __threadfence_system();
   cluster_sync_all();  // every peer has finished reading this CTA's partial
 
   tc_fence_before();
@@ -865,7 +875,7 @@ bool gemm_tc_supported(const void* x, int64_t ldx, int K, const GemmSeg* segs, i
 
 int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int nseg, int epi,
             const float* bias, void* y, int64_t ldy, int y_dtype, void* ws, size_t ws_bytes,
-            int32_t* status, cudaStream_t s) {
+            int32_t* status, cudaStream_t s, const Scatter* sc) {
   B2_CHECK_ARG(nseg >= 1 && nseg <= tc::kMaxSegs, "gemm_tc: bad segment count");
   B2_CHECK_ARG(gemm_tc_supported(x, ldx, K, segs, nseg),
                "gemm_tc: needs K %% 8 == 0, 16-byte aligned rows (K=%d ldx=%lld)", K, (long long)ldx);
@@ -901,6 +911,12 @@ int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int n
     p.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + tc::kCounterBytes);
   }
   p.status = status;
+  if (sc && sc->world > 0) {
+    p.sc_table = sc->table;
+    p.sc_R = sc->rows_per_rank;
+    p.sc_src = sc->src;
+    p.sc_world = sc->world;
+  }
 
   CUtensorMap mx, mw[3];
   int rc = tc::make_map(&mx, x, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 2, (uint32_t)pl.BN);

@@ -113,13 +113,54 @@ class DistributedLLaMAModel(nn.Module):
     def dtype(self) -> torch.dtype:
         return self.embed_tokens.weight.dtype
 
+    def _forward_hidden_sharded(self, ids: torch.Tensor, md: TokenMetadata, kv_pool: PhysicalKVCachePool,
+                                trace: Optional[list]) -> torch.Tensor:
+        """Tensor-parallel layers with a row-sharded residual (world_size > 1).
+
+        Each rank keeps the float32 residual only for its rows; every row-parallel GEMM
+        pushes its partial rows to their owners from its epilogue, and the owners finish
+        the all-reduce, add the residual, normalise and all-gather the normalised rows
+        into every rank's buffer (``b2_row_parallel_linear`` + ``b2_allreduce_rmsnorm_sharded``).
+        """
+        cfg, comm = self.config, self.communicator
+        eps = cfg.rms_norm_eps
+        T, H = md.n_tokens, cfg.hidden_dim
+        wdt = self.dtype
+        h_all = kernels.embedding(ids, self.embed_tokens.weight, out_dtype=torch.float32)
+        xn = torch.empty(T, H, dtype=wdt, device=self.device)
+        kernels.rmsnorm(h_all, self.layers[0].input_layernorm.weight, eps, out=xn)
+        r0, r1, R = comm.row_slice(T)
+        h = torch.zeros(R, H, dtype=torch.float32, device=self.device)
+        if r1 > r0:
+            h[: r1 - r0].copy_(h_all[r0:r1])
+        n = len(self.layers)
+        for i, layer in enumerate(self.layers):
+            attn = layer.self_attn.attend(xn, md, kv_pool)
+            par = comm.next_parity()
+            comm.row_parallel_linear(par, attn, layer.self_attn.out_proj.packed_weight())
+            xn = comm.allreduce_rmsnorm_sharded(par, T, H, wdt, h, layer.post_attention_layernorm.weight, eps)
+            inter = layer.mlp.gate_up(xn)
+            next_w = self.layers[i + 1].input_layernorm.weight if i + 1 < n else self.norm.weight
+            par = comm.next_parity()
+            comm.row_parallel_linear(par, inter, layer.mlp.down_proj.packed_weight())
+            xn = comm.allreduce_rmsnorm_sharded(par, T, H, wdt, h, next_w, eps)
+            if trace is not None:
+                trace.append((r0, h[: r1 - r0].clone()))
+        return xn
+
     def forward_hidden(self, token_ids: torch.Tensor, md: TokenMetadata, kv_pool: PhysicalKVCachePool,
                        trace: Optional[list] = None) -> torch.Tensor:
         """Runs every layer; returns the final-normed hidden states [T, hidden] in the model dtype.
 
         ``trace`` (optional list) receives a copy of the float32 residual stream after
-        each layer (the reference block's output), for parity checks.
+        each layer (the reference block's output), for parity checks; with
+        world_size > 1 each entry is ``(first_row, rows)`` of this rank's row slice.
         """
+        if self.world_size > 1 and self.communicator is not None:
+            ids = token_ids.reshape(-1)
+            if ids.device != self.device or ids.dtype != torch.int64:
+                ids = ids.to(self.device, torch.int64)
+            return self._forward_hidden_sharded(ids, md, kv_pool, trace)
         cfg = self.config
         eps = cfg.rms_norm_eps
         T, H = md.n_tokens, cfg.hidden_dim

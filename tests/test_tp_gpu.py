@@ -176,7 +176,9 @@ def _tp_layer_worker(rank, world, port, out_dir):
     toks = torch.randint(0, cfg.vocab_size, (1, 40), generator=torch.Generator().manual_seed(5))
     tr = []
     logits = model(toks.to(dev), torch.arange(40)[None], pool, [[3, 9, 1]], True, 0, trace=tr)
-    np.save(os.path.join(out_dir, f"h_rank{rank}.npy"), tr[0].cpu().numpy())
+    r0, h_slice = tr[0]
+    np.save(os.path.join(out_dir, f"h_rank{rank}.npy"), h_slice.cpu().numpy())
+    np.save(os.path.join(out_dir, f"r0_rank{rank}.npy"), np.asarray([r0]))
     np.save(os.path.join(out_dir, f"logits_rank{rank}.npy"), logits.cpu().numpy())
     dist.barrier()
     comm.cleanup()
@@ -188,8 +190,9 @@ def test_llama3_8b_shape_layer_tp2_matches_oracle(tmp_path):
     import oracle
     from pythonintern_b200 import workloads
     mp.start_processes(_tp_layer_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
-    h0, h1 = np.load(tmp_path / "h_rank0.npy"), np.load(tmp_path / "h_rank1.npy")
-    assert np.array_equal(h0, h1)
+    # each rank holds the residual of its own rows: rows [0, 20) and [20, 40)
+    assert int(np.load(tmp_path / "r0_rank0.npy")[0]) == 0 and int(np.load(tmp_path / "r0_rank1.npy")[0]) == 20
+    h0 = np.concatenate([np.load(tmp_path / "h_rank0.npy"), np.load(tmp_path / "h_rank1.npy")])
     assert np.array_equal(np.load(tmp_path / "logits_rank0.npy"), np.load(tmp_path / "logits_rank1.npy"))
     cfg = workloads.llama3_8b_config(num_layers=1, max_seq_len=512)
     cfg.vocab_size = 4096
