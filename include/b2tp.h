@@ -204,26 +204,23 @@ int b2_allreduce_rmsnorm(b2_comm* comm, int parity, int rows, int dim, int dtype
 /* Row-parallel linear fused with the reduce-scatter of its all-reduce
  * (RowParallelLinear.forward, engine/tensor_parallel/layers.py:147-158): the partial
  * y = x.w^T is computed on this rank and row m of it is stored, straight from the GEMM
- * epilogue, into the data buffer `parity` of rank m / R (R = ceil(M / world)) at row
+ * epilogue, into the current receive slot of rank m / R (R = ceil(M / world)) at row
  * (this rank * R + m % R); rows owned by peers travel over NVLink while the GEMM runs.
- * The matching b2_allreduce_rmsnorm_sharded call completes the all-reduce. */
-int b2_row_parallel_linear(b2_comm* comm, int parity, const void* x, int64_t ldx, int M, int K, const void* w,
-                           int N, int dtype, void* workspace, size_t workspace_bytes, int32_t* status,
+ * The next b2_allreduce_rmsnorm_sharded call on the same communicator completes it. */
+int b2_row_parallel_linear(b2_comm* comm, const void* x, int64_t ldx, int M, int K, const void* w, int N,
+                           int dtype, void* workspace, size_t workspace_bytes, int32_t* status,
                            b2_stream_t stream);
 
 /* Completes the all-reduce of b2_row_parallel_linear for a row-sharded residual
  * (comm.py:72-118 + llama.py:70,75 + the next RMSNorm, layers.py:179-184): this rank
  * owns rows [rank*R, rank*R + R) of the [rows, dim] activations and keeps their float32
- * residual in h_slice [R, dim].  h_slice += sum over ranks (in rank order) of their
- * partial rows; the rows are normalised by norm_w and pushed into EVERY rank's xn
- * buffer `parity` (b2_comm_xn_buffer), so that on return all ranks hold the full
- * [rows, dim] normalised activations for the next column-parallel GEMM.  Two flag
- * barriers, each bounded by timeout_ns. */
-int b2_allreduce_rmsnorm_sharded(b2_comm* comm, int parity, int rows, int dim, int dtype, float* h_slice,
-                                 const float* norm_w, float eps, int64_t timeout_ns, int32_t* status,
-                                 b2_stream_t stream);
-/* Device pointer of this rank's all-gather buffer `parity` of normalised rows. */
-int b2_comm_xn_buffer(b2_comm* comm, int parity, void** ptr);
+ * residual in h_slice [R, dim].  h_slice += the sum over ranks (rank order) of their
+ * partial rows; the rows are normalised by norm_w and pushed to every rank, and on
+ * return y [rows, dim] holds all normalised rows on every rank.  No flags: every
+ * element's arrival is detected in sentinel-filled rotating slots, each wait bounded
+ * by timeout_ns. */
+int b2_allreduce_rmsnorm_sharded(b2_comm* comm, int rows, int dim, int dtype, float* h_slice, const float* norm_w,
+                                 float eps, void* y, int64_t timeout_ns, int32_t* status, b2_stream_t stream);
 
 #ifdef __cplusplus
 }

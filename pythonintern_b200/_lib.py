@@ -66,11 +66,10 @@ _SIGS = {
     "b2_allreduce_sum": (_c_int, [_c_void_p, _c_int, _c_size, _c_int, _c_void_p, _c_i64, _c_void_p, _c_void_p]),
     "b2_allreduce_rmsnorm": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
                                       _c_void_p, _c_float, _c_void_p, _c_int, _c_i64, _c_void_p, _c_void_p]),
-    "b2_row_parallel_linear": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_i64, _c_int, _c_int, _c_void_p,
-                                        _c_int, _c_int, _c_void_p, _c_size, _c_void_p, _c_void_p]),
-    "b2_allreduce_rmsnorm_sharded": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_void_p,
-                                              _c_void_p, _c_float, _c_i64, _c_void_p, _c_void_p]),
-    "b2_comm_xn_buffer": (_c_int, [_c_void_p, _c_int, ctypes.POINTER(_c_void_p)]),
+    "b2_row_parallel_linear": (_c_int, [_c_void_p, _c_void_p, _c_i64, _c_int, _c_int, _c_void_p, _c_int,
+                                        _c_int, _c_void_p, _c_size, _c_void_p, _c_void_p]),
+    "b2_allreduce_rmsnorm_sharded": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
+                                              _c_float, _c_void_p, _c_i64, _c_void_p, _c_void_p]),
 }
 
 _lib: Optional[ctypes.CDLL] = None

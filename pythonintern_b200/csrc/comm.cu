@@ -16,6 +16,12 @@
 //      0..world-1 in float32 (so all ranks produce bit-identical results),
 //   4. (fused variant) adds the float32 residual, writes it back, and applies the
 //      next RMSNorm (layers.py:179-184).
+// The fused row-parallel path (b2_row_parallel_linear + b2_allreduce_rmsnorm_sharded)
+// uses no flags at all: its receive buffers rotate over three slots chosen by the device
+// epoch and are filled with a sentinel (all-ones bytes, a NaN payload that arithmetic
+// never produces) when idle, so the arrival of every element is its own signal.  A
+// slot is refilled with the sentinel one call after it was consumed, which leaves a
+// full call of slack before any rank can write it again.
 // The epoch is a device-side counter advanced by the last CTA of every call, so
 // CUDA-graph replays need no host bookkeeping.  Two data buffers alternate by call
 // parity: a rank can only start overwriting data[p] after every peer has raised
@@ -32,11 +38,15 @@ namespace b2 {
 constexpr int kMaxRanks = 8;
 constexpr int kMaxCtas = 128;
 
+constexpr int kSlots = 3;  // rotating receive slots of the flag-free fused path
+
 struct CommView {
-  void* data[2][kMaxRanks];     // every rank's data (receive) buffers (own included)
-  void* xn[2][kMaxRanks];       // every rank's all-gather buffers of normalised rows
-  uint32_t* flags[kMaxRanks];   // every rank's flag array [2 phases][kMaxRanks][kMaxCtas]
-  uint32_t* ctrl;               // own {epoch, done}
+  void* data[2][kMaxRanks];        // every rank's one-shot data buffers (own included)
+  void* xn[kSlots][kMaxRanks];     // every rank's all-gather slots of normalised rows
+  void* recv_own[kSlots];          // this rank's reduce-scatter receive slots
+  uint32_t* flags[kMaxRanks];      // every rank's flag array [kMaxRanks][kMaxCtas]
+  uint32_t* ctrl;                  // own {epoch, done}
+  size_t slot_bytes;
   int rank, world;
 };
 
@@ -45,8 +55,8 @@ struct CommView {
 struct b2_comm {
   int rank, world, device;
   size_t max_bytes, data_bytes;
-  size_t off_data[2], off_xn[2], off_flags, off_ctrl, off_table, total;
-  unsigned long long* scatter_table;  // device: [2 parities][kMaxRanks] peer data buffer addresses
+  size_t off_data[2], off_recv[b2::kSlots], off_xn[b2::kSlots], off_flags, off_ctrl, off_table, total;
+  unsigned long long* scatter_table;  // device: [kSlots][kMaxRanks] every rank's receive slot addresses
   char* base;                       // own allocation
   char* peer_base[b2::kMaxRanks];   // mapped peers (own base at [rank])
   cudaIpcMemHandle_t handle;
@@ -65,13 +75,11 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-// Steps 1-2 of the protocol (flag set `phase`).  Returns false (and raises the status
-// bit) on timeout.
-__device__ bool comm_barrier(const CommView& v, uint32_t epoch, int64_t timeout_ns, int32_t* status,
-                             int phase = 0) {
+// Steps 1-2 of the flag protocol.  Returns false (and raises the status bit) on timeout.
+__device__ bool comm_barrier(const CommView& v, uint32_t epoch, int64_t timeout_ns, int32_t* status) {
   __shared__ int s_ok;
   const int cta = blockIdx.x;
-  const int pofs = phase * kMaxRanks * kMaxCtas;
+  const int pofs = 0;
   if (threadIdx.x == 0) s_ok = 1;
   __syncthreads();
   if (threadIdx.x < v.world) {
@@ -210,66 +218,152 @@ __global__ void allreduce_rmsnorm_kernel(CommView v, int parity, int rows, int d
   comm_finish(v);
 }
 
-// Second half of the row-parallel all-reduce with a row-sharded residual.  The partials
-// were pushed by the row-parallel GEMM of every rank into this rank's data buffer as
-// [src][R][dim] (R = rows per rank).  After barrier 0, each CTA takes owned rows
-// (global row = rank * R + lr): h = h_slice + sum over src (rank order), h_slice = h,
-// y = rmsnorm(h) * w, and pushes y into row `row` of EVERY rank's xn buffer.  Barrier 1
-// then guarantees that all rows of the xn buffer are in place on every rank.
+// Sentinel helpers: a slot element still equal to the all-ones pattern has not arrived.
+__device__ __forceinline__ uint4 ld_volatile16(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
 template <typename T>
-__global__ void allreduce_rmsnorm_sharded_kernel(CommView v, int parity, int rows, int R, int dim,
-                                                 float* h_slice, const float* __restrict__ w, float eps,
-                                                 int64_t timeout_ns, int32_t* status) {
-  __shared__ float red[32];
-  const uint32_t epoch = v.ctrl[0] + 1;
-  bool ok = comm_barrier(v, epoch, timeout_ns, status, 0);
-  const int nv = dim / 8;
-  if (ok) {
-    const T* recv = reinterpret_cast<const T*>(v.data[parity][v.rank]);
-    for (int lr = blockIdx.x; lr < R; lr += gridDim.x) {
-      const int row = v.rank * R + lr;
-      if (row >= rows) break;  // uniform across the CTA
-      float hv[4][8];
-      float ss = 0.f;
+__device__ __forceinline__ bool has_sentinel(const uint4& v) {
+  if (sizeof(T) == 4) return v.x == 0xffffffffu || v.y == 0xffffffffu || v.z == 0xffffffffu || v.w == 0xffffffffu;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        const int j = threadIdx.x + it * blockDim.x;
-        if (j >= nv) continue;
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int src = 0; src < v.world; ++src) {
-          float x[8];
-          load8<T>(recv + ((size_t)src * R + lr) * dim + j * 8, x);
+  for (int k = 0; k < 4; ++k)
+    if ((w[k] & 0xffffu) == 0xffffu || (w[k] >> 16) == 0xffffu) return true;
+  return false;
+}
+// Waits (bounded by deadline) until the 16 bytes at p hold no sentinel element.
+template <typename T>
+__device__ __forceinline__ uint4 wait16(const void* p, uint64_t deadline, bool* ok) {
+  uint4 v = ld_volatile16(p);
+  uint32_t it = 0;
+  while (has_sentinel<T>(v)) {
+    if ((++it & 63) == 0 && globaltimer_ns() > deadline) {
+      *ok = false;
+      return v;
+    }
+    v = ld_volatile16(p);
+  }
+  return v;
+}
+__device__ __forceinline__ void unpack8(const uint4& raw, float (&o)[8], bool bf16) {
+  if (bf16) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] += x[e];
-        }
-        float* hp = h_slice + (size_t)lr * dim + j * 8;
-        const float4 h0 = *reinterpret_cast<const float4*>(hp);
-        const float4 h1 = *reinterpret_cast<const float4*>(hp + 4);
-        const float hr[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          hv[it][e] = hr[e] + acc[e];
-          ss += hv[it][e] * hv[it][e];
-        }
-        *reinterpret_cast<float4*>(hp) = make_float4(hv[it][0], hv[it][1], hv[it][2], hv[it][3]);
-        *reinterpret_cast<float4*>(hp + 4) = make_float4(hv[it][4], hv[it][5], hv[it][6], hv[it][7]);
-      }
-      ss = block_sum(ss, red);
-      const float inv = rsqrtf(ss / (float)dim + eps);
-#pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        const int j = threadIdx.x + it * blockDim.x;
-        if (j >= nv) continue;
-        float o[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = hv[it][e] * inv * w[j * 8 + e];
-        for (int q = 0; q < v.world; ++q)  // all-gather by posted stores (own buffer included)
-          store8<T>(reinterpret_cast<T*>(v.xn[parity][q]) + (size_t)row * dim + j * 8, o);
-      }
-      __syncthreads();
+    for (int i = 0; i < 4; ++i) {
+      o[2 * i] = __uint_as_float(w[i] << 16);
+      o[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
     }
   }
-  if (ok) ok = comm_barrier(v, epoch, timeout_ns, status, 1);
+}
+
+// Second half of the fused row-parallel all-reduce (flag free).  Slot b = epoch % 3.
+//  A. CTA c < R owns row rank*R + c: it waits for each source's partial row in its receive
+//     slot b, sums them in rank order, adds the float32 residual slice, normalises, and
+//     stores the normalised row into slot b of EVERY rank's all-gather buffer.
+//  B. every CTA refills its share of the slots used by the previous call ((b + 2) % 3)
+//     with the sentinel.
+//  C. every CTA waits for its share of rows of its own all-gather slot b and copies them
+//     to y (the caller's [rows, dim] output).
+template <typename T>
+__global__ void allreduce_rmsnorm_sharded_kernel(CommView v, int rows, int R, int dim, float* h_slice,
+                                                 const float* __restrict__ w, float eps, T* __restrict__ y,
+                                                 int64_t timeout_ns, int32_t* status) {
+  __shared__ float red[32];
+  __shared__ int s_ok;
+  const uint32_t epoch = v.ctrl[0];
+  const int b = (int)(epoch % kSlots);
+  const int prev = (b + kSlots - 1) % kSlots;
+  const uint64_t deadline = globaltimer_ns() + (uint64_t)timeout_ns;
+  const int nv = dim / 8;
+  constexpr bool BF = sizeof(T) == 2;
+  bool ok = true;
+  if (threadIdx.x == 0) s_ok = 1;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    v.ctrl[2 + b] = (uint32_t)(((size_t)v.world * R * dim * sizeof(T)) / 16);
+    v.ctrl[5 + b] = (uint32_t)(((size_t)rows * dim * sizeof(T)) / 16);
+  }
+  __syncthreads();
+
+  // A. reduce the owned row
+  const int row = v.rank * R + blockIdx.x;
+  if (blockIdx.x < R && row < rows) {
+    const T* recv = reinterpret_cast<const T*>(v.recv_own[b]);
+    float hv[4][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int j = threadIdx.x + it * blockDim.x;
+      if (j >= nv) continue;
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int src = 0; src < v.world; ++src) {
+        const T* ptr = recv + ((size_t)src * R + blockIdx.x) * dim + j * 8;
+        float x[8];
+        if (BF) {
+          const uint4 raw = wait16<T>(ptr, deadline, &ok);
+          unpack8(raw, x, true);
+        } else {
+          const uint4 r0 = wait16<T>(ptr, deadline, &ok);
+          const uint4 r1 = wait16<T>(ptr + 4, deadline, &ok);
+          x[0] = __uint_as_float(r0.x); x[1] = __uint_as_float(r0.y); x[2] = __uint_as_float(r0.z); x[3] = __uint_as_float(r0.w);
+          x[4] = __uint_as_float(r1.x); x[5] = __uint_as_float(r1.y); x[6] = __uint_as_float(r1.z); x[7] = __uint_as_float(r1.w);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += x[e];
+      }
+      float* hp = h_slice + (size_t)blockIdx.x * dim + j * 8;
+      const float4 h0 = *reinterpret_cast<const float4*>(hp);
+      const float4 h1 = *reinterpret_cast<const float4*>(hp + 4);
+      const float hr[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        hv[it][e] = hr[e] + acc[e];
+        ss += hv[it][e] * hv[it][e];
+      }
+      *reinterpret_cast<float4*>(hp) = make_float4(hv[it][0], hv[it][1], hv[it][2], hv[it][3]);
+      *reinterpret_cast<float4*>(hp + 4) = make_float4(hv[it][4], hv[it][5], hv[it][6], hv[it][7]);
+    }
+    ss = block_sum(ss, red);
+    const float inv = rsqrtf(ss / (float)dim + eps);
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int j = threadIdx.x + it * blockDim.x;
+      if (j >= nv) continue;
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = hv[it][e] * inv * w[j * 8 + e];
+      for (int q = 0; q < v.world; ++q)
+        store8<T>(reinterpret_cast<T*>(v.xn[b][q]) + (size_t)row * dim + j * 8, o);
+    }
+  }
+
+  // B. re-arm the previous call's slots (receive slot and own all-gather slot) over the
+  //    extents that call used, which ctrl[2 + slot] / ctrl[5 + slot] record in 16-byte units.
+  {
+    const size_t recv_n16 = v.ctrl[2 + prev];
+    const size_t xn_n16 = v.ctrl[5 + prev];
+    uint4* r16 = reinterpret_cast<uint4*>(v.recv_own[prev]);
+    uint4* x16 = reinterpret_cast<uint4*>(v.xn[prev][v.rank]);
+    const uint4 ones = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < recv_n16; i += (size_t)gridDim.x * blockDim.x)
+      r16[i] = ones;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < xn_n16; i += (size_t)gridDim.x * blockDim.x)
+      x16[i] = ones;
+  }
+
+  // C. wait for the all-gathered rows and copy them out
+  {
+    const uint4* xs = reinterpret_cast<const uint4*>(v.xn[b][v.rank]);
+    uint4* yd = reinterpret_cast<uint4*>(y);
+    const size_t n16 = ((size_t)rows * dim * sizeof(T)) / 16;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x)
+      yd[i] = wait16<T>(xs + i, deadline, &ok);
+  }
+  if (!ok) {
+    raise_status(status, B2_DEV_PEER_TIMEOUT);
+    s_ok = 0;
+  }
   comm_finish(v);
 }
 
@@ -280,10 +374,11 @@ static CommView make_view(const b2_comm* c) {
   for (int r = 0; r < c->world; ++r) {
     v.data[0][r] = c->peer_base[r] + c->off_data[0];
     v.data[1][r] = c->peer_base[r] + c->off_data[1];
-    v.xn[0][r] = c->peer_base[r] + c->off_xn[0];
-    v.xn[1][r] = c->peer_base[r] + c->off_xn[1];
+    for (int k = 0; k < kSlots; ++k) v.xn[k][r] = c->peer_base[r] + c->off_xn[k];
     v.flags[r] = reinterpret_cast<uint32_t*>(c->peer_base[r] + c->off_flags);
   }
+  for (int k = 0; k < kSlots; ++k) v.recv_own[k] = c->base + c->off_recv[k];
+  v.slot_bytes = c->data_bytes;
   v.ctrl = reinterpret_cast<uint32_t*>(c->base + c->off_ctrl);
   return v;
 }
@@ -292,10 +387,10 @@ static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Fills the device table of every rank's data-buffer address (as seen from this rank).
 static int fill_scatter_table(b2_comm* c) {
-  unsigned long long t[2 * kMaxRanks] = {0};
-  for (int par = 0; par < 2; ++par)
+  unsigned long long t[kSlots * kMaxRanks] = {0};
+  for (int k = 0; k < kSlots; ++k)
     for (int r = 0; r < c->world; ++r)
-      t[par * kMaxRanks + r] = (unsigned long long)(uintptr_t)(c->peer_base[r] + c->off_data[par]);
+      t[k * kMaxRanks + r] = (unsigned long long)(uintptr_t)(c->peer_base[r] + c->off_recv[k]);
   int dev = 0;
   B2_TRY_CUDA(cudaGetDevice(&dev));
   B2_TRY_CUDA(cudaSetDevice(c->device));
@@ -325,10 +420,12 @@ int b2_comm_create(int rank, int world_size, size_t max_bytes, b2_comm** out) {
   c->data_bytes = b2::align_up(max_bytes, 4096);
   c->off_data[0] = 0;
   c->off_data[1] = c->data_bytes;
-  c->off_xn[0] = 2 * c->data_bytes;
-  c->off_xn[1] = 3 * c->data_bytes;
-  c->off_flags = 4 * c->data_bytes;
-  c->off_ctrl = c->off_flags + b2::align_up((size_t)2 * b2::kMaxRanks * b2::kMaxCtas * sizeof(uint32_t), 256);
+  for (int k = 0; k < b2::kSlots; ++k) {
+    c->off_recv[k] = (2 + k) * c->data_bytes;
+    c->off_xn[k] = (2 + b2::kSlots + k) * c->data_bytes;
+  }
+  c->off_flags = (2 + 2 * b2::kSlots) * c->data_bytes;
+  c->off_ctrl = c->off_flags + b2::align_up((size_t)b2::kMaxRanks * b2::kMaxCtas * sizeof(uint32_t), 256);
   c->off_table = c->off_ctrl + 256;
   c->total = c->off_table + 256;
   cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&c->base), c->total);
@@ -337,7 +434,9 @@ int b2_comm_create(int rank, int world_size, size_t max_bytes, b2_comm** out) {
     return b2::fail(B2_ECUDA, "b2_comm_create: cudaMalloc(%zu): %s", (size_t)0, cudaGetErrorString(e));
   }
   e = cudaMemset(c->base + c->off_flags, 0, c->total - c->off_flags);
-  if (e == cudaSuccess) e = cudaMemset(c->base, 0, 4 * c->data_bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->base, 0, 2 * c->data_bytes);
+  // idle receive and all-gather slots hold the sentinel
+  if (e == cudaSuccess) e = cudaMemset(c->base + c->off_recv[0], 0xff, 2 * b2::kSlots * c->data_bytes);
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&c->handle, c->base);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
@@ -441,12 +540,6 @@ int b2_comm_buffer(b2_comm* comm, int parity, void** ptr) {
   return B2_OK;
 }
 
-int b2_comm_xn_buffer(b2_comm* comm, int parity, void** ptr) {
-  B2_CHECK_ARG(comm && ptr && (parity == 0 || parity == 1), "b2_comm_xn_buffer: bad arguments");
-  *ptr = comm->base + comm->off_xn[parity];
-  return B2_OK;
-}
-
 int b2_comm_destroy(b2_comm* comm) {
   if (!comm) return B2_OK;
   int dev = 0;
@@ -514,11 +607,10 @@ int b2_allreduce_rmsnorm(b2_comm* comm, int parity, int rows, int dim, int dtype
   return B2_OK;
 }
 
-int b2_row_parallel_linear(b2_comm* comm, int parity, const void* x, int64_t ldx, int M, int K, const void* w,
-                           int N, int dtype, void* workspace, size_t workspace_bytes, int32_t* status,
+int b2_row_parallel_linear(b2_comm* comm, const void* x, int64_t ldx, int M, int K, const void* w, int N,
+                           int dtype, void* workspace, size_t workspace_bytes, int32_t* status,
                            b2_stream_t stream) {
   B2_CHECK_ARG(comm && comm->opened, "b2_row_parallel_linear: communicator not opened");
-  B2_CHECK_ARG(parity == 0 || parity == 1, "b2_row_parallel_linear: parity must be 0 or 1");
   B2_CHECK_ARG(b2::valid_dtype(dtype), "b2_row_parallel_linear: bad dtype");
   B2_CHECK_ARG(M >= 0 && K > 0 && N > 0 && ldx >= K, "b2_row_parallel_linear: bad sizes");
   if (M == 0) return B2_OK;
@@ -526,18 +618,17 @@ int b2_row_parallel_linear(b2_comm* comm, int parity, const void* x, int64_t ldx
   const int R = (M + comm->world - 1) / comm->world;
   B2_CHECK_ARG((size_t)comm->world * R * N * b2::dtype_bytes(dtype) <= comm->max_bytes,
                "b2_row_parallel_linear: %d x %d partial exceeds the communicator buffer", M, N);
-  b2::Scatter sc{comm->scatter_table + parity * b2::kMaxRanks, R, comm->rank, comm->world};
+  b2::Scatter sc{comm->scatter_table, reinterpret_cast<const unsigned int*>(comm->base + comm->off_ctrl), R,
+                 comm->rank, comm->world};
   if (dtype == B2_F32) return b2::gemm_simt(x, ldx, M, K, w, nullptr, N, nullptr, nullptr, N, dtype, dtype, stream, &sc);
   b2::GemmSeg seg{w, N, 0};
   return b2::gemm_tc(x, ldx, M, K, &seg, 1, b2::kEpiStore, nullptr, nullptr, N, dtype, workspace, workspace_bytes,
                      status, stream, &sc);
 }
 
-int b2_allreduce_rmsnorm_sharded(b2_comm* comm, int parity, int rows, int dim, int dtype, float* h_slice,
-                                 const float* norm_w, float eps, int64_t timeout_ns, int32_t* status,
-                                 b2_stream_t stream) {
+int b2_allreduce_rmsnorm_sharded(b2_comm* comm, int rows, int dim, int dtype, float* h_slice, const float* norm_w,
+                                 float eps, void* y, int64_t timeout_ns, int32_t* status, b2_stream_t stream) {
   B2_CHECK_ARG(comm && comm->opened, "b2_allreduce_rmsnorm_sharded: communicator not opened");
-  B2_CHECK_ARG(parity == 0 || parity == 1, "b2_allreduce_rmsnorm_sharded: parity must be 0 or 1");
   B2_CHECK_ARG(b2::valid_dtype(dtype), "b2_allreduce_rmsnorm_sharded: bad dtype");
   B2_CHECK_ARG(rows >= 0 && dim > 0 && dim % 8 == 0 && dim <= 8 * 4 * 512,
                "b2_allreduce_rmsnorm_sharded: bad dim %d", dim);
@@ -545,19 +636,21 @@ int b2_allreduce_rmsnorm_sharded(b2_comm* comm, int parity, int rows, int dim, i
   const int R = (rows + comm->world - 1) / comm->world;
   B2_CHECK_ARG((size_t)comm->world * R * dim * b2::dtype_bytes(dtype) <= comm->max_bytes,
                "b2_allreduce_rmsnorm_sharded: payload exceeds the buffer");
-  B2_CHECK_ARG(norm_w && (h_slice || comm->rank * R >= rows), "b2_allreduce_rmsnorm_sharded: null pointer");
-  B2_CHECK_ARG(((uintptr_t)h_slice % 16) == 0 && ((uintptr_t)norm_w % 16) == 0,
-               "b2_allreduce_rmsnorm_sharded: h_slice and norm_w must be 16-byte aligned");
+  B2_CHECK_ARG(norm_w && y && (h_slice || comm->rank * R >= rows), "b2_allreduce_rmsnorm_sharded: null pointer");
+  B2_CHECK_ARG(((uintptr_t)h_slice % 16) == 0 && ((uintptr_t)norm_w % 16) == 0 && ((uintptr_t)y % 16) == 0,
+               "b2_allreduce_rmsnorm_sharded: h_slice, norm_w and y must be 16-byte aligned");
   const b2::CommView v = b2::make_view(comm);
-  const int grid = R < b2::kMaxCtas ? R : b2::kMaxCtas;
+  int grid = R < 32 ? 32 : R;
+  if (grid > b2::kMaxCtas) grid = b2::kMaxCtas;
+  B2_CHECK_ARG(R <= grid, "b2_allreduce_rmsnorm_sharded: %d rows per rank exceed %d", R, b2::kMaxCtas);
   int threads = 64;
   while (threads < 512 && threads * 4 < dim / 8) threads *= 2;
   if (dtype == B2_BF16)
     b2::allreduce_rmsnorm_sharded_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
-        v, parity, rows, R, dim, h_slice, norm_w, eps, timeout_ns, status);
+        v, rows, R, dim, h_slice, norm_w, eps, (__nv_bfloat16*)y, timeout_ns, status);
   else
     b2::allreduce_rmsnorm_sharded_kernel<float><<<grid, threads, 0, stream>>>(
-        v, parity, rows, R, dim, h_slice, norm_w, eps, timeout_ns, status);
+        v, rows, R, dim, h_slice, norm_w, eps, (float*)y, timeout_ns, status);
   B2_TRY_CUDA(cudaGetLastError());
   return B2_OK;
 }

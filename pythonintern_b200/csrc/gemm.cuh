@@ -19,10 +19,12 @@ struct GemmSeg {
 };
 
 // Reduce-scatter destination of a row-parallel GEMM: output row m goes to rank
-// o = m / rows_per_rank, at row (src * rows_per_rank + m % rows_per_rank) of the buffer
-// whose device address is table[o] (peer memory for o != src).  world == 0: plain output.
+// o = m / rows_per_rank, at row (src * rows_per_rank + m % rows_per_rank) of the receive
+// slot whose device address is table[(*epoch % 3) * 8 + o] (peer memory for o != src).
+// world == 0: plain output.
 struct Scatter {
   const unsigned long long* table;
+  const unsigned int* epoch;
   int rows_per_rank, src, world;
 };
 
@@ -32,11 +34,12 @@ int gemm_simt(const void* x, int64_t ldx, int M, int K, const void* w0, const vo
 
 // Address of output element (m, col) for a plain or scattered destination.
 __device__ __forceinline__ void* out_base(void* y, int y_dtype, int64_t ldy, const unsigned long long* table,
-                                          int R, int src, int world, int64_t m, int64_t col, int64_t* idx) {
+                                          const unsigned int* epoch, int R, int src, int world, int64_t m,
+                                          int64_t col, int64_t* idx) {
   if (world > 0) {
     const int o = (int)(m / R);
     *idx = ((int64_t)src * R + (m - (int64_t)o * R)) * ldy + col;
-    return reinterpret_cast<void*>(table[o]);
+    return reinterpret_cast<void*>(table[(*epoch % 3u) * 8u + o]);
   }
   *idx = m * ldy + col;
   return y;

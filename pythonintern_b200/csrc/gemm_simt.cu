@@ -78,17 +78,16 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
         if (bias) v += bias[n];
       }
       int64_t idx;
-      void* base = out_base(Y, y_dtype, ldy, sc.table, sc.rows_per_rank, sc.src, sc.world, m, n, &idx);
+      void* base = out_base(Y, y_dtype, ldy, sc.table, sc.epoch, sc.rows_per_rank, sc.src, sc.world, m, n, &idx);
       st_dyn(base, y_dtype, idx, v);
     }
   }
-  if (sc.world > 0) __threadfence_system();
 }
 
 int gemm_simt(const void* x, int64_t ldx, int M, int K, const void* w0, const void* w1, int N,
               const float* bias, void* y, int64_t ldy, int dtype, int y_dtype, cudaStream_t s,
               const Scatter* scp) {
-  const Scatter sc = scp ? *scp : Scatter{nullptr, 1, 0, 0};
+  const Scatter sc = scp ? *scp : Scatter{nullptr, nullptr, 1, 0, 0};
   dim3 grid((N + SBN - 1) / SBN, (M + SBM - 1) / SBM);
   B2_CHECK_ARG(grid.y <= 65535, "gemm: M=%d too large", M);
   if (dtype == B2_BF16) {

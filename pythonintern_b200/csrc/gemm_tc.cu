@@ -49,12 +49,13 @@ struct Params {
   int* counters;
   int32_t* status;
   const unsigned long long* sc_table;  // reduce-scatter destinations (sc_world > 0)
+  const unsigned int* sc_epoch;
   int sc_R, sc_src, sc_world;
 };
 
 __device__ __forceinline__ void store_out(const Params& p, int64_t m, int64_t col, float v) {
   int64_t idx;
-  void* base = out_base(p.y, p.y_dtype, p.ldy, p.sc_table, p.sc_R, p.sc_src, p.sc_world, m, col, &idx);
+  void* base = out_base(p.y, p.y_dtype, p.ldy, p.sc_table, p.sc_epoch, p.sc_R, p.sc_src, p.sc_world, m, col, &idx);
   st_dyn(base, p.y_dtype, idx, v);
 }
 
@@ -480,9 +481,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ---------------- teardown
-  // Scattered rows were stored into peer memory: make them visible system-wide before the
-  // CTA retires, so the consumer's flag barrier (after this kernel) orders them.
-  if (p.sc_world > 0) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -679,7 +677,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       store_out(p, m0 + c, seg_col + nb + e, val);
     }
   }
-  if (p.sc_world > 0) __threadfence_system();
   cluster_sync_all();  // every peer has finished reading this CTA's partial
 
   tc_fence_before();
@@ -913,6 +910,7 @@ int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int n
   p.status = status;
   if (sc && sc->world > 0) {
     p.sc_table = sc->table;
+    p.sc_epoch = sc->epoch;
     p.sc_R = sc->rows_per_rank;
     p.sc_src = sc->src;
     p.sc_world = sc->world;

@@ -136,14 +136,12 @@ class DistributedLLaMAModel(nn.Module):
         n = len(self.layers)
         for i, layer in enumerate(self.layers):
             attn = layer.self_attn.attend(xn, md, kv_pool)
-            par = comm.next_parity()
-            comm.row_parallel_linear(par, attn, layer.self_attn.out_proj.packed_weight())
-            xn = comm.allreduce_rmsnorm_sharded(par, T, H, wdt, h, layer.post_attention_layernorm.weight, eps)
+            comm.row_parallel_linear(attn, layer.self_attn.out_proj.packed_weight())
+            xn = comm.allreduce_rmsnorm_sharded(T, H, wdt, h, layer.post_attention_layernorm.weight, eps)
             inter = layer.mlp.gate_up(xn)
             next_w = self.layers[i + 1].input_layernorm.weight if i + 1 < n else self.norm.weight
-            par = comm.next_parity()
-            comm.row_parallel_linear(par, inter, layer.mlp.down_proj.packed_weight())
-            xn = comm.allreduce_rmsnorm_sharded(par, T, H, wdt, h, next_w, eps)
+            comm.row_parallel_linear(inter, layer.mlp.down_proj.packed_weight())
+            xn = comm.allreduce_rmsnorm_sharded(T, H, wdt, h, next_w, eps)
             if trace is not None:
                 trace.append((r0, h[: r1 - r0].clone()))
         return xn

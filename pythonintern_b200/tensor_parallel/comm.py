@@ -189,26 +189,6 @@ class DistributedCommunicator:
             self._views[key] = view
         return view
 
-    def xn_buffer(self, parity: int, shape, dtype: torch.dtype) -> torch.Tensor:
-        """This rank's all-gather buffer ``parity`` of normalised rows, viewed as ``shape``."""
-        shape = tuple(int(s) for s in shape)
-        key = ("xn", parity, shape, dtype)
-        view = self._views.get(key)
-        if view is None:
-            n = 1
-            for s in shape:
-                n *= s
-            nbytes = n * torch.tensor([], dtype=dtype).element_size()
-            if nbytes > self.max_bytes:
-                raise ValueError(f"{nbytes}-byte activations exceed the {self.max_bytes}-byte buffer")
-            self._ensure_created()
-            out = ctypes.c_void_p()
-            check(_lib.lib().b2_comm_xn_buffer(self._comm, parity, ctypes.byref(out)), "b2_comm_xn_buffer")
-            raw = torch.as_tensor(_DevicePointer(out.value, nbytes), device=self.device)
-            view = raw.view(dtype).view(*shape)
-            self._views[key] = view
-        return view
-
     def row_slice(self, rows: int):
         """Rows [start, end) of a [rows, dim] activation this rank owns in the sharded all-reduce."""
         R = (rows + self.world_size - 1) // self.world_size
@@ -216,33 +196,6 @@ class DistributedCommunicator:
         return start, min(rows, start + R), R
 
     # ------------------------------------------------------------------ collectives
-    def row_parallel_linear(self, parity: int, x: torch.Tensor, w_packed: torch.Tensor):
-        """Row-parallel GEMM whose epilogue pushes each output row to the rank that owns it."""
-        self._require_open()
-        K = x.shape[-1]
-        x2 = x if (x.dim() == 2 and x.stride(1) == 1) else x.reshape(-1, K).contiguous()
-        M, N = x2.shape[0], w_packed.shape[0]
-        dc = dtype_code(w_packed.dtype)
-        nbytes = _lib.lib().b2_linear_workspace_bytes(M, N, K, dc)
-        ws = _lib.workspace(self.device, "linear", nbytes)
-        check(_lib.lib().b2_row_parallel_linear(self._comm, parity, ptr(x2), x2.stride(0), M, K, ptr(w_packed), N,
-                                                dc, ptr(ws), nbytes, status_ptr(self.device),
-                                                stream_ptr(self.device)), "b2_row_parallel_linear")
-
-    def allreduce_rmsnorm_sharded(self, parity: int, rows: int, dim: int, dtype: torch.dtype,
-                                  h_slice: torch.Tensor, norm_w: torch.Tensor, eps: float,
-                                  timeout_sec: float = 15.0) -> torch.Tensor:
-        """Completes ``row_parallel_linear``: residual slice += sum of partials, normalise, all-gather.
-
-        Returns the [rows, dim] normalised activations (this rank's xn buffer ``parity``).
-        """
-        self._require_open()
-        check(_lib.lib().b2_allreduce_rmsnorm_sharded(self._comm, parity, rows, dim, dtype_code(dtype),
-                                                      ptr(h_slice), ptr(norm_w), float(eps),
-                                                      int(timeout_sec * 1e9), status_ptr(self.device),
-                                                      stream_ptr(self.device)), "b2_allreduce_rmsnorm_sharded")
-        return self.xn_buffer(parity, (rows, dim), dtype)
-
     def all_reduce_sum(self, tensor: torch.Tensor, step_tag: str = "", timeout_sec: float = 15.0) -> torch.Tensor:
         """Synchronous all-reduce(SUM); returns a new tensor (comm.py:72-118)."""
         if self.world_size <= 1:
@@ -278,6 +231,35 @@ class DistributedCommunicator:
                                               ptr(h_out), ptr(norm_w), float(eps), ptr(y), dtype_code(y.dtype),
                                               int(timeout_sec * 1e9), status_ptr(self.device),
                                               stream_ptr(self.device)), "b2_allreduce_rmsnorm")
+
+    def row_parallel_linear(self, x: torch.Tensor, w_packed: torch.Tensor):
+        """Row-parallel GEMM whose epilogue pushes each output row to the rank that owns it."""
+        self._require_open()
+        K = x.shape[-1]
+        x2 = x if (x.dim() == 2 and x.stride(1) == 1) else x.reshape(-1, K).contiguous()
+        M, N = x2.shape[0], w_packed.shape[0]
+        dc = dtype_code(w_packed.dtype)
+        nbytes = _lib.lib().b2_linear_workspace_bytes(M, N, K, dc)
+        ws = _lib.workspace(self.device, "linear", nbytes)
+        check(_lib.lib().b2_row_parallel_linear(self._comm, ptr(x2), x2.stride(0), M, K, ptr(w_packed), N, dc,
+                                                ptr(ws), nbytes, status_ptr(self.device),
+                                                stream_ptr(self.device)), "b2_row_parallel_linear")
+
+    def allreduce_rmsnorm_sharded(self, rows: int, dim: int, dtype: torch.dtype, h_slice: torch.Tensor,
+                                  norm_w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None,
+                                  timeout_sec: float = 15.0) -> torch.Tensor:
+        """Completes ``row_parallel_linear``: residual slice += sum of partials, normalise, all-gather.
+
+        Returns the [rows, dim] normalised activations (every rank gets all rows).
+        """
+        self._require_open()
+        if out is None:
+            out = torch.empty(rows, dim, dtype=dtype, device=self.device)
+        check(_lib.lib().b2_allreduce_rmsnorm_sharded(self._comm, rows, dim, dtype_code(dtype), ptr(h_slice),
+                                                      ptr(norm_w), float(eps), ptr(out), int(timeout_sec * 1e9),
+                                                      status_ptr(self.device), stream_ptr(self.device)),
+              "b2_allreduce_rmsnorm_sharded")
+        return out
 
     def cleanup(self):
         """Release the symmetric buffers and peer mappings (comm.py:156-166)."""
