@@ -407,7 +407,8 @@ def run_ours(args):
     peak, peak_kind = measured_peaks()
     dk = kern[dominant]
     roofline = {"bound": "hbm", "kernel": dominant, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
-                "frac": dk["gbs"] / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "frac": dk["gbs"] / peak, "peak_source": ("measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                                else "fallback (6.65 TB/s, an earlier copy measurement on these B200s)"),
                 "traffic": None, "algorithmic_bytes_per_launch": dk["bytes"],
                 "share_of_step": per_step[dominant] / 1000.0 / (ms / K)}
 

@@ -267,7 +267,7 @@ __device__ __forceinline__ void unpack8(const uint4& raw, float (&o)[8], bool bf
 //  C. every CTA waits for its share of rows of its own all-gather slot b and copies them
 //     to y (the caller's [rows, dim] output).
 template <typename T>
-__global__ void allreduce_rmsnorm_sharded_kernel(CommView v, int rows, int R, int dim, float* h_slice,
+__global__ void __launch_bounds__(512) allreduce_rmsnorm_sharded_kernel(CommView v, int rows, int R, int dim, float* h_slice,
                                                  const float* __restrict__ w, float eps, T* __restrict__ y,
                                                  int64_t timeout_ns, int32_t* status) {
   __shared__ float red[32];
@@ -291,30 +291,48 @@ __global__ void allreduce_rmsnorm_sharded_kernel(CommView v, int rows, int R, in
   if (blockIdx.x < R && row < rows) {
     const T* recv = reinterpret_cast<const T*>(v.recv_own[b]);
     float hv[4][8];
+    float4 wv[4][2];
     float ss = 0.f;
 #pragma unroll
     for (int it = 0; it < 4; ++it) {
       const int j = threadIdx.x + it * blockDim.x;
       if (j >= nv) continue;
+      // residual and norm weight are requested first; they do not depend on the partials
+      float* hp = h_slice + (size_t)blockIdx.x * dim + j * 8;
+      const float4 h0 = *reinterpret_cast<const float4*>(hp);
+      const float4 h1 = *reinterpret_cast<const float4*>(hp + 4);
+      wv[it][0] = __ldg(reinterpret_cast<const float4*>(w + j * 8));
+      wv[it][1] = __ldg(reinterpret_cast<const float4*>(w + j * 8) + 1);
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int src = 0; src < v.world; ++src) {
+      // every source's vector is loaded before any is checked, so the common case costs
+      // one round of independent loads; only vectors that have not arrived are polled again
+      constexpr int NV16 = BF ? 1 : 2;  // 16-byte loads per 8 elements
+      uint4 raw[NV16 * kMaxRanks];
+#pragma unroll
+      for (int src = 0; src < kMaxRanks; ++src) {
+        if (src >= v.world) break;
         const T* ptr = recv + ((size_t)src * R + blockIdx.x) * dim + j * 8;
+#pragma unroll
+        for (int h = 0; h < NV16; ++h) raw[src * NV16 + h] = ld_volatile16(ptr + h * (8 / NV16));
+      }
+#pragma unroll
+      for (int src = 0; src < kMaxRanks; ++src) {
+        if (src >= v.world) break;
+        const T* ptr = recv + ((size_t)src * R + blockIdx.x) * dim + j * 8;
+#pragma unroll
+        for (int h = 0; h < NV16; ++h)
+          if (has_sentinel<T>(raw[src * NV16 + h])) raw[src * NV16 + h] = wait16<T>(ptr + h * (8 / NV16), deadline, &ok);
         float x[8];
         if (BF) {
-          const uint4 raw = wait16<T>(ptr, deadline, &ok);
-          unpack8(raw, x, true);
+          unpack8(raw[src * NV16], x, true);
         } else {
-          const uint4 r0 = wait16<T>(ptr, deadline, &ok);
-          const uint4 r1 = wait16<T>(ptr + 4, deadline, &ok);
+          const uint4 r0 = raw[src * NV16], r1 = raw[src * NV16 + NV16 - 1];
           x[0] = __uint_as_float(r0.x); x[1] = __uint_as_float(r0.y); x[2] = __uint_as_float(r0.z); x[3] = __uint_as_float(r0.w);
           x[4] = __uint_as_float(r1.x); x[5] = __uint_as_float(r1.y); x[6] = __uint_as_float(r1.z); x[7] = __uint_as_float(r1.w);
         }
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[e] += x[e];
       }
-      float* hp = h_slice + (size_t)blockIdx.x * dim + j * 8;
-      const float4 h0 = *reinterpret_cast<const float4*>(hp);
-      const float4 h1 = *reinterpret_cast<const float4*>(hp + 4);
       const float hr[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -330,9 +348,11 @@ __global__ void allreduce_rmsnorm_sharded_kernel(CommView v, int rows, int R, in
     for (int it = 0; it < 4; ++it) {
       const int j = threadIdx.x + it * blockDim.x;
       if (j >= nv) continue;
+      const float wr[8] = {wv[it][0].x, wv[it][0].y, wv[it][0].z, wv[it][0].w,
+                           wv[it][1].x, wv[it][1].y, wv[it][1].z, wv[it][1].w};
       float o[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = hv[it][e] * inv * w[j * 8 + e];
+      for (int e = 0; e < 8; ++e) o[e] = hv[it][e] * inv * wr[e];
       for (int q = 0; q < v.world; ++q)
         store8<T>(reinterpret_cast<T*>(v.xn[b][q]) + (size_t)row * dim + j * 8, o);
     }
@@ -352,13 +372,25 @@ __global__ void allreduce_rmsnorm_sharded_kernel(CommView v, int rows, int R, in
       x16[i] = ones;
   }
 
-  // C. wait for the all-gathered rows and copy them out
+  // C. wait for the all-gathered rows and copy them out, four independent loads per round
   {
     const uint4* xs = reinterpret_cast<const uint4*>(v.xn[b][v.rank]);
     uint4* yd = reinterpret_cast<uint4*>(y);
     const size_t n16 = ((size_t)rows * dim * sizeof(T)) / 16;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x)
-      yd[i] = wait16<T>(xs + i, deadline, &ok);
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n16; i0 += 4 * stride) {
+      uint4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u * stride < n16) r[u] = ld_volatile16(xs + i0 + u * stride);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const size_t i = i0 + u * stride;
+        if (i >= n16) break;
+        if (has_sentinel<T>(r[u])) r[u] = wait16<T>(xs + i, deadline, &ok);
+        yd[i] = r[u];
+      }
+    }
   }
   if (!ok) {
     raise_status(status, B2_DEV_PEER_TIMEOUT);
@@ -640,11 +672,11 @@ int b2_allreduce_rmsnorm_sharded(b2_comm* comm, int rows, int dim, int dtype, fl
   B2_CHECK_ARG(((uintptr_t)h_slice % 16) == 0 && ((uintptr_t)norm_w % 16) == 0 && ((uintptr_t)y % 16) == 0,
                "b2_allreduce_rmsnorm_sharded: h_slice, norm_w and y must be 16-byte aligned");
   const b2::CommView v = b2::make_view(comm);
-  int grid = R < 32 ? 32 : R;
+  int grid = R < 64 ? 64 : R;
   if (grid > b2::kMaxCtas) grid = b2::kMaxCtas;
   B2_CHECK_ARG(R <= grid, "b2_allreduce_rmsnorm_sharded: %d rows per rank exceed %d", R, b2::kMaxCtas);
-  int threads = 64;
-  while (threads < 512 && threads * 4 < dim / 8) threads *= 2;
+  int threads = 64;  // one 8-element vector per thread per row up to dim 4096
+  while (threads < 512 && threads < dim / 8) threads *= 2;
   if (dtype == B2_BF16)
     b2::allreduce_rmsnorm_sharded_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
         v, rows, R, dim, h_slice, norm_w, eps, (__nv_bfloat16*)y, timeout_ns, status);

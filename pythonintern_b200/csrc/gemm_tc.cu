@@ -31,6 +31,10 @@ namespace tc {
 constexpr int BM = 128;  // weight rows per tile (MMA M)
 constexpr int BK = 64;   // K elements per stage = one 128-byte swizzle atom
 constexpr int kThreads = 192;  // 6 warps: producer, MMA, 4 epilogue
+// Cluster split-K kernel: producer, MMA, 8 warps that publish the partial tile (two per
+// TMEM lane quarter) and 2 more; all 12 warps share the reduction, which is bound by
+// the number of L2 loads in flight.
+constexpr int kThreadsCl = 384;
 constexpr int kMaxSegs = 3;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on any pipeline wait
 
@@ -51,12 +55,28 @@ struct Params {
   const unsigned long long* sc_table;  // reduce-scatter destinations (sc_world > 0)
   const unsigned int* sc_epoch;
   int sc_R, sc_src, sc_world;
+  int vec4;  // output columns in aligned groups of 4: store 4 elements per instruction
 };
 
 __device__ __forceinline__ void store_out(const Params& p, int64_t m, int64_t col, float v) {
   int64_t idx;
   void* base = out_base(p.y, p.y_dtype, p.ldy, p.sc_table, p.sc_epoch, p.sc_R, p.sc_src, p.sc_world, m, col, &idx);
   st_dyn(base, p.y_dtype, idx, v);
+}
+// Four consecutive output columns col..col+3 of row m (p.vec4: col % 4 == 0, aligned rows):
+// one 8-byte (bf16) or 16-byte (float32) store, which keeps peer-memory writes whole.
+__device__ __forceinline__ void store_out4(const Params& p, int64_t m, int64_t col, const float (&v)[4]) {
+  int64_t idx;
+  void* base = out_base(p.y, p.y_dtype, p.ldy, p.sc_table, p.sc_epoch, p.sc_R, p.sc_src, p.sc_world, m, col, &idx);
+  if (p.y_dtype == B2_BF16) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]), hi = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&lo);
+    o.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(base) + idx) = o;
+  } else {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + idx) = make_float4(v[0], v[1], v[2], v[3]);
+  }
 }
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -156,6 +176,24 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
       : "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 lanes x 32 consecutive 32-bit columns; waits for the load before returning.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row core
@@ -467,11 +505,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
             const float uv[4] = {u4.x, u4.y, u4.z, u4.w};
+            float val[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              if (nb + e >= seg_n) continue;
-              const float val = SWIGLU ? silu_f32(gv[e]) * uv[e] : gv[e] + bv[e];
-              store_out(p, m0 + c, seg_col + nb + e, val);
+            for (int e = 0; e < 4; ++e) val[e] = SWIGLU ? silu_f32(gv[e]) * uv[e] : gv[e] + bv[e];
+            if (p.vec4 && nb + 3 < seg_n) {
+              store_out4(p, m0 + c, seg_col + nb, val);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                if (nb + e < seg_n) store_out(p, m0 + c, seg_col + nb + e, val[e]);
             }
           }
         }
@@ -490,12 +532,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------
-// Split-K with the reduction in distributed shared memory.  One thread-block cluster per
-// output tile, one CTA per K split (cluster rank = split).  After its mainloop each CTA
-// copies its float32 partial tile from TMEM into its (now idle) pipeline shared memory;
-// after a cluster barrier, CTA k sums column slice k of every CTA's partial through
-// DSMEM (mapa + ld.shared::cluster) and stores that slice; a second cluster barrier keeps
-// every CTA resident until its partial has been read.
+// Split-K over a thread-block cluster.  One cluster per output tile, one CTA per K split
+// (cluster rank = split).  After its mainloop each CTA writes its float32 partial tile
+// from TMEM to its own workspace region; after one cluster barrier (release / acquire at
+// cluster scope), CTA k sums column slice k of every CTA's partial, read from L2 in split
+// order, and stores that slice.  The cluster only guarantees that the CTAs of a tile are
+// resident together, so the barrier cannot wait on a CTA that was never scheduled.
+constexpr int kMaxClusterSplits = 8;  // portable cluster size: split-K of at most 8
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -504,27 +547,13 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-__device__ __forceinline__ uint32_t map_to_cta(uint32_t local_smem, uint32_t cta) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem), "r"(cta));
-  return r;
-}
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
-  return v;
-}
-
 template <int BN, bool SWIGLU>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsCl, 1)
     gemm_tc_cluster_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW0,
                            const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmW2,
                            const Params p) {
   using C = Cfg<BN, SWIGLU>;
   constexpr int STAGES = C::STAGES;
-  constexpr int PARTS = SWIGLU ? 2 : 1;
-  static_assert((size_t)PARTS * BN * BM * 4 <= (size_t)STAGES * C::STAGE_BYTES, "partial tile must fit the ring");
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
@@ -629,55 +658,88 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   }
 
-  // Stage the partial tile [part][column][128 rows] in this CTA's shared memory.
-  float* stage = reinterpret_cast<float*>(smem);
-  if (warp >= 2) {
-    const int quarter = warp & 3;
+  // Publish this CTA's float32 partial tile ([part][column][128 rows]) to its workspace
+  // region straight from TMEM; after the cluster barrier every CTA reduces its slice of
+  // token columns over the partials of all the cluster's CTAs, in split order, from L2.
+  constexpr int PARTS = SWIGLU ? 2 : 1;
+  constexpr int64_t PART_ELEMS = (int64_t)PARTS * BN * BM;
+  const int64_t cta_lin = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
+  if (warp >= 2 && warp < 10) {
+    const int quarter = warp & 3;          // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;      // alternate 16-column chunks between two warps
     const int r = quarter * 32 + lane;
     const uint32_t acc = tmem + ((uint32_t)(quarter * 32) << 16);
+    float* mine = p.ws + cta_lin * PART_ELEMS;
     const bool done = mbar_wait(&acc_full, 0);
     if (!done && lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
     tc_fence_after();
-    for (int c0 = 0; c0 < ncols; c0 += 16) {
 #pragma unroll
-      for (int part = 0; part < PARTS; ++part) {
+    for (int part = 0; part < PARTS; ++part) {
+      for (int c0 = 16 * half; c0 < ncols; c0 += 32) {
         float v[16];
         tmem_ld16(acc + part * BN + c0, v);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) stage[(part * BN + c0 + e) * BM + r] = done ? v[e] : 0.f;
+        for (int e = 0; e < 16; ++e) mine[(part * BN + c0 + e) * BM + r] = done ? v[e] : 0.f;
       }
     }
   }
-  cluster_sync_all();
+  cluster_sync_all();  // release / acquire at cluster scope: every partial of the cluster is visible
 
-  // Reduce this CTA's column slice over every split's partial, then store it.
+  const float* part0 = p.ws + (cta_lin - split) * PART_ELEMS;  // split 0 of this tile
   const int per = (ncols + p.splits - 1) / p.splits;
   const int c_lo = split * per, c_hi = min(ncols, c_lo + per);
-  const int r4 = lane * 4;
-  const int nb = local_tile * BM + r4;
-  const uint32_t stage_u32 = smem_u32(stage);
-  for (int c = c_lo + warp; c < c_hi; c += kThreads / 32) {
-    float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), u4 = g4;
-    for (int q = 0; q < p.splits; ++q) {
-      const uint32_t base = map_to_cta(stage_u32, (uint32_t)q);
-      const float4 a = ld_dsmem_f4(base + (uint32_t)((c * BM + r4) * 4));
-      g4.x += a.x; g4.y += a.y; g4.z += a.z; g4.w += a.w;
-      if (SWIGLU) {
-        const float4 b = ld_dsmem_f4(base + (uint32_t)(((BN + c) * BM + r4) * 4));
-        u4.x += b.x; u4.y += b.y; u4.z += b.z; u4.w += b.w;
+  constexpr int VPC = BM / 4;  // float4 vectors per token column
+  constexpr int U = SWIGLU ? 1 : 2;  // vectors per thread whose loads are all issued first
+  const int nvec = (c_hi > c_lo ? c_hi - c_lo : 0) * VPC;
+  for (int i0 = threadIdx.x; i0 < nvec; i0 += U * kThreadsCl) {
+    float4 ga[U][kMaxClusterSplits], ua[U][SWIGLU ? kMaxClusterSplits : 1];
+#pragma unroll
+    for (int h = 0; h < U; ++h) {
+      const int i = i0 + h * kThreadsCl;
+      if (i >= nvec) continue;
+      const float* src = part0 + (int64_t)(c_lo + i / VPC) * BM + (i % VPC) * 4;
+#pragma unroll
+      for (int q = 0; q < kMaxClusterSplits; ++q) {
+        if (q < p.splits) {
+          ga[h][q] = __ldcg(reinterpret_cast<const float4*>(src + q * PART_ELEMS));
+          if (SWIGLU) ua[h][q] = __ldcg(reinterpret_cast<const float4*>(src + q * PART_ELEMS + (int64_t)BN * BM));
+        }
       }
     }
-    const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
-    const float uv[4] = {u4.x, u4.y, u4.z, u4.w};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (nb + e >= seg_n) continue;
-      const float bv = (!SWIGLU && p.bias) ? p.bias[seg_col + nb + e] : 0.f;
-      const float val = SWIGLU ? silu_f32(gv[e]) * uv[e] : gv[e] + bv;
-      store_out(p, m0 + c, seg_col + nb + e, val);
+    for (int h = 0; h < U; ++h) {
+      const int i = i0 + h * kThreadsCl;
+      if (i >= nvec) continue;
+      const int c = c_lo + i / VPC;
+      const int r4 = (i % VPC) * 4;
+      float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), u4 = g4;
+#pragma unroll
+      for (int q = 0; q < kMaxClusterSplits; ++q) {
+        if (q < p.splits) {
+          g4.x += ga[h][q].x; g4.y += ga[h][q].y; g4.z += ga[h][q].z; g4.w += ga[h][q].w;
+          if (SWIGLU) {
+            u4.x += ua[h][q].x; u4.y += ua[h][q].y; u4.z += ua[h][q].z; u4.w += ua[h][q].w;
+          }
+        }
+      }
+      const int nb = local_tile * BM + r4;
+      const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+      const float uv[4] = {u4.x, u4.y, u4.z, u4.w};
+      float val[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float bv = (!SWIGLU && p.bias && nb + e < seg_n) ? p.bias[seg_col + nb + e] : 0.f;
+        val[e] = SWIGLU ? silu_f32(gv[e]) * uv[e] : gv[e] + bv;
+      }
+      if (p.vec4 && nb + 3 < seg_n) {
+        store_out4(p, m0 + c, seg_col + nb, val);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (nb + e < seg_n) store_out(p, m0 + c, seg_col + nb + e, val[e]);
+      }
     }
   }
-  cluster_sync_all();  // every peer has finished reading this CTA's partial
 
   tc_fence_before();
   __syncthreads();
@@ -716,21 +778,23 @@ static int make_map(CUtensorMap* m, const void* ptr, uint64_t k, uint64_t rows, 
   return B2_OK;
 }
 
-// The DSMEM split-K path stages the float32 partial tile in the idle pipeline ring.
+// The cluster split-K path serves token tiles of up to 128 columns.
 #define BN_FITS_CLUSTER(bn, swiglu) ((bn) <= 128)
 
 struct Plan {
   int BN, m_tiles, n_tiles, nkb, splits, kbps, ctas;
-  bool cluster;  // split-K reduced through DSMEM (one cluster per tile) instead of the workspace
+  bool cluster;  // split-K over one thread-block cluster per tile (else the persistent kernel)
 };
 
 // Launch plan.  Measured on B200 over the decode shapes (M = 1..128 tokens; q|k|v,
 // o_proj, gate|up, down of the 8B shape): when the output has at least half as many
 // 128-row tiles as there are SMs, the persistent kernel without split-K streams best;
-// otherwise split K over a thread-block cluster of s CTAs per tile, reduced in DSMEM,
-// with the largest s in {8, 4, 2} whose CTAs fit in one wave (clusters of 3, 5 or 6
-// schedule measurably worse).  The persistent split-K path with a global workspace
-// remains for token tiles too wide for the DSMEM staging (BN = 256).
+// otherwise split K over a thread-block cluster of s CTAs per tile, with the largest s
+// in {8, 4, 2} whose CTAs fit in one wave (clusters of 3, 5 or 6 schedule measurably
+// worse).  The cluster's CTAs exchange float32 partials through an L2 workspace and one
+// cluster barrier, each reducing 1/s of the token columns; an exchange through
+// distributed shared memory measured about twice as slow.  The persistent split-K path
+// (last CTA of a tile reduces) remains for token tiles wider than 128 (BN = 256).
 static Plan make_plan(int M, int n_tiles, int K, bool swiglu) {
   Plan pl{};
   pl.BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
@@ -765,7 +829,7 @@ constexpr size_t kCounterSlots = 65536;
 constexpr size_t kCounterBytes = kCounterSlots * sizeof(int);
 
 static size_t plan_ws_bytes(const Plan& pl, bool swiglu) {
-  if (pl.splits <= 1 || pl.cluster) return 0;
+  if (pl.splits <= 1) return 0;
   const size_t tiles = (size_t)pl.n_tiles * pl.m_tiles;
   return kCounterBytes + (size_t)pl.splits * tiles * (swiglu ? 2 : 1) * BM * pl.BN * sizeof(float);
 }
@@ -801,7 +865,7 @@ static int launch_cluster(const CUtensorMap& mx, const CUtensorMap& w0, const CU
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(p.n_tiles * p.splits), (unsigned)p.m_tiles, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(kThreadsCl, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -908,6 +972,12 @@ int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int n
     p.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + tc::kCounterBytes);
   }
   p.status = status;
+  {
+    const size_t esz = y_dtype == B2_BF16 ? 2 : 4;
+    bool v4 = ldy % 4 == 0 && (sc && sc->world > 0 ? true : ((uintptr_t)y % (4 * esz)) == 0);
+    for (int i = 0; i < nseg; ++i) v4 = v4 && segs[i].col_off % 4 == 0 && segs[i].n % 4 == 0;
+    p.vec4 = v4 ? 1 : 0;
+  }
   if (sc && sc->world > 0) {
     p.sc_table = sc->table;
     p.sc_epoch = sc->epoch;

@@ -4,15 +4,20 @@
 module tree and parameter names (so ``state_dict`` keys match the reference and
 its WeightSharder), and the reference's forward signatures.
 
-``DistributedLLaMAModel.forward`` runs the fused path: the residual stream stays
-float32 in HBM and each row-parallel projection is followed by ONE kernel that
-all-reduces (NVLink peer loads when world_size > 1), adds the residual and applies
-the NEXT RMSNorm (the post-attention norm, the next layer's input norm, or the
-final norm), so a decoder layer is seven kernels:
+``DistributedLLaMAModel.forward`` runs the fused path.  The residual stream stays
+float32 in HBM, and each row-parallel projection is followed by ONE kernel that finishes
+the all-reduce, adds the residual and applies the NEXT RMSNorm (the post-attention norm,
+the next layer's input norm, or the final norm), so a decoder layer is seven kernels:
 
     qkv GEMM -> RoPE + KV write -> paged attention -> o_proj GEMM
     -> all-reduce + residual + norm -> gate/up GEMM + SwiGLU -> down GEMM
     -> all-reduce + residual + norm
+
+With world_size > 1 the residual is sharded by rows: each rank keeps the float32
+residual of its own rows only, the row-parallel GEMM pushes each partial row to the rank
+that owns it straight from its epilogue (NVLink stores into peer memory), and the owner
+sums, normalises and pushes the normalised row to every rank (all-gather), all inside
+``b2_row_parallel_linear`` + ``b2_allreduce_rmsnorm_sharded``.
 """
 
 from __future__ import annotations
@@ -34,18 +39,10 @@ from pythonintern_b200._lib import torch_dtype
 
 
 def _row_parallel_norm(proj: RowParallelLinear, inp: torch.Tensor, h: torch.Tensor, norm_w: torch.Tensor,
-                       eps: float, y: torch.Tensor, comm: Optional[DistributedCommunicator]):
-    """``h += AllReduce(inp @ W)``; ``y = rmsnorm(h) * norm_w`` (layers.py:147-162 + llama.py:70-75)."""
-    T, H = h.shape
-    wdt = proj.weight.dtype
-    if proj.world_size > 1 and comm is not None:
-        parity = comm.next_parity()
-        partial = comm.partial_buffer(parity, (T, H), wdt)
-        kernels.linear(inp, proj.packed_weight(), out=partial)
-        comm.allreduce_rmsnorm(parity, T, H, wdt, h, h, norm_w, eps, y)
-    else:
-        partial = kernels.linear(inp, proj.packed_weight())
-        kernels.rmsnorm(partial, norm_w, eps, residual=h, h_out=h, out=y)
+                       eps: float, y: torch.Tensor):
+    """``h += inp @ W``; ``y = rmsnorm(h) * norm_w`` at world_size 1 (layers.py:147-162 + llama.py:70-75)."""
+    partial = kernels.linear(inp, proj.packed_weight())
+    kernels.rmsnorm(partial, norm_w, eps, residual=h, h_out=h, out=y)
 
 
 class DistributedTransformerBlock(nn.Module):
@@ -154,7 +151,9 @@ class DistributedLLaMAModel(nn.Module):
         each layer (the reference block's output), for parity checks; with
         world_size > 1 each entry is ``(first_row, rows)`` of this rank's row slice.
         """
-        if self.world_size > 1 and self.communicator is not None:
+        if self.world_size > 1:
+            if self.communicator is None:
+                raise RuntimeError("world_size > 1 needs a communicator (set_communicator)")
             ids = token_ids.reshape(-1)
             if ids.device != self.device or ids.dtype != torch.int64:
                 ids = ids.to(self.device, torch.int64)
@@ -163,7 +162,6 @@ class DistributedLLaMAModel(nn.Module):
         eps = cfg.rms_norm_eps
         T, H = md.n_tokens, cfg.hidden_dim
         wdt = self.dtype
-        comm = self.communicator if self.world_size > 1 else None
         ids = token_ids.reshape(-1)
         if ids.device != self.device or ids.dtype != torch.int64:
             ids = ids.to(self.device, torch.int64)
@@ -173,11 +171,10 @@ class DistributedLLaMAModel(nn.Module):
         n = len(self.layers)
         for i, layer in enumerate(self.layers):
             attn = layer.self_attn.attend(xn, md, kv_pool)
-            _row_parallel_norm(layer.self_attn.out_proj, attn, h, layer.post_attention_layernorm.weight, eps, xn,
-                               comm)
+            _row_parallel_norm(layer.self_attn.out_proj, attn, h, layer.post_attention_layernorm.weight, eps, xn)
             inter = layer.mlp.gate_up(xn)
             next_w = self.layers[i + 1].input_layernorm.weight if i + 1 < n else self.norm.weight
-            _row_parallel_norm(layer.mlp.down_proj, inter, h, next_w, eps, xn, comm)
+            _row_parallel_norm(layer.mlp.down_proj, inter, h, next_w, eps, xn)
             if trace is not None:
                 trace.append(h.clone())
         return xn

@@ -308,8 +308,6 @@ def test_decode_graph_replay_matches_eager():
         outs.append(hist)
     for (ta, la), (tb, lb) in zip(*outs):
         assert ta == tb
-        # the graph sizes its attention split count for the bucket's width, so the split
-        # merge order may differ from the eager call and flip bf16 roundings: compare at
-        # the bf16 tolerance
-        la, lb = np.asarray(la), np.asarray(lb)
-        assert np.linalg.norm(la - lb) / np.linalg.norm(lb) < 2e-2
+        # eager and graph pick the same attention split count (same table bucket), so
+        # the logits are bit-identical
+        np.testing.assert_array_equal(np.asarray(la), np.asarray(lb))
