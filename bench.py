@@ -43,6 +43,12 @@ if ROOT not in sys.path:
 
 HBM_FALLBACK_GBS = 6650.0
 
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) over the
+# algorithmic bytes of the same launch, from one ncu capture of the attention kernel at
+# batch 128, context 2048: 1.0887 GB measured for 1.0884 GB algorithmic.  Traffic grows with the KV bytes read,
+# so other batch sizes, contexts and TP degrees scale it by their algorithmic bytes.
+MEASURED_TRAFFIC_RATIO = {"paged_attention": 1.0887e9 / 1088421888}
+
 
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -409,7 +415,11 @@ def run_ours(args):
     roofline = {"bound": "hbm", "kernel": dominant, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
                 "frac": dk["gbs"] / peak, "peak_source": ("measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                                 else "fallback (6.65 TB/s, an earlier copy measurement on these B200s)"),
-                "traffic": None, "algorithmic_bytes_per_launch": dk["bytes"],
+                "traffic": (MEASURED_TRAFFIC_RATIO[dominant] * dk["bytes"]
+                            if dominant in MEASURED_TRAFFIC_RATIO else None),
+                "traffic_source": ("ncu capture at batch 128, context 2048, TP=1, scaled by algorithmic bytes"
+                                   if dominant in MEASURED_TRAFFIC_RATIO else None),
+                "algorithmic_bytes_per_launch": dk["bytes"],
                 "share_of_step": per_step[dominant] / 1000.0 / (ms / K)}
 
     # ---------------- fused all-reduce + residual + RMSNorm bus bandwidth (TP > 1)
