@@ -167,6 +167,8 @@ __device__ void attn_finalize(const AttnParams& p, const float* sm_m, const floa
 
 template <typename T, int HD, int REP>
 __global__ void __launch_bounds__(kAttnWarps * 32) paged_attn_simt_kernel(AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int VEC = 16 / sizeof(T);
   constexpr int LPT = HD / VEC;  // lanes per token row
   constexpr int G = 32 / LPT;    // token rows per warp step
@@ -375,6 +377,8 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
 
 template <int HD, int REP>
 __global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
   using C = MmaCfg<HD>;
   static_assert(REP <= 8, "the MMA tile holds up to 8 query heads per kv head");
   extern __shared__ __align__(128) uint8_t smem[];
@@ -544,18 +548,19 @@ static int allow_dynamic_smem(const void* fn, size_t bytes) {
 template <int HD>
 static int launch_mma_rep(int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {
   using C = MmaCfg<HD>;
-  auto set = [&](const void* fn) -> int { return allow_dynamic_smem(fn, C::SMEM); };
-  int rc = B2_OK;
+  auto go = [&](void (*k)(AttnParams)) -> int {
+    const int rc = allow_dynamic_smem((const void*)k, C::SMEM);
+    if (rc) return rc;
+    B2_TRY_CUDA(launch_pdl(k, grid, dim3(kMmaWarps * 32), C::SMEM, s, p));
+    return B2_OK;
+  };
   switch (rep) {
-    case 1: rc = set((const void*)paged_attn_mma_kernel<HD, 1>); if (!rc) paged_attn_mma_kernel<HD, 1><<<grid, kMmaWarps * 32, C::SMEM, s>>>(p); break;
-    case 2: rc = set((const void*)paged_attn_mma_kernel<HD, 2>); if (!rc) paged_attn_mma_kernel<HD, 2><<<grid, kMmaWarps * 32, C::SMEM, s>>>(p); break;
-    case 4: rc = set((const void*)paged_attn_mma_kernel<HD, 4>); if (!rc) paged_attn_mma_kernel<HD, 4><<<grid, kMmaWarps * 32, C::SMEM, s>>>(p); break;
-    case 8: rc = set((const void*)paged_attn_mma_kernel<HD, 8>); if (!rc) paged_attn_mma_kernel<HD, 8><<<grid, kMmaWarps * 32, C::SMEM, s>>>(p); break;
+    case 1: return go(paged_attn_mma_kernel<HD, 1>);
+    case 2: return go(paged_attn_mma_kernel<HD, 2>);
+    case 4: return go(paged_attn_mma_kernel<HD, 4>);
+    case 8: return go(paged_attn_mma_kernel<HD, 8>);
     default: return fail(B2_ENOTSUP, "b2_paged_attention: nq/nkv = %d not supported (1, 2, 4, 8)", rep);
   }
-  if (rc) return rc;
-  B2_TRY_CUDA(cudaGetLastError());
-  return B2_OK;
 }
 
 static int launch_mma(int hd, int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {
@@ -588,15 +593,17 @@ static AttnWs attn_ws_layout(int n_rows, int nq, int nkv, int hd, int splits) {
 
 template <typename T, int HD>
 static int launch_rep(int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {
+  auto go = [&](void (*k)(AttnParams)) -> int {
+    B2_TRY_CUDA(launch_pdl(k, grid, dim3(kAttnWarps * 32), 0, s, p));
+    return B2_OK;
+  };
   switch (rep) {
-    case 1: paged_attn_simt_kernel<T, HD, 1><<<grid, kAttnWarps * 32, 0, s>>>(p); break;
-    case 2: paged_attn_simt_kernel<T, HD, 2><<<grid, kAttnWarps * 32, 0, s>>>(p); break;
-    case 4: paged_attn_simt_kernel<T, HD, 4><<<grid, kAttnWarps * 32, 0, s>>>(p); break;
-    case 8: paged_attn_simt_kernel<T, HD, 8><<<grid, kAttnWarps * 32, 0, s>>>(p); break;
+    case 1: return go(paged_attn_simt_kernel<T, HD, 1>);
+    case 2: return go(paged_attn_simt_kernel<T, HD, 2>);
+    case 4: return go(paged_attn_simt_kernel<T, HD, 4>);
+    case 8: return go(paged_attn_simt_kernel<T, HD, 8>);
     default: return fail(B2_ENOTSUP, "b2_paged_attention: nq/nkv = %d not supported (1, 2, 4, 8)", rep);
   }
-  B2_TRY_CUDA(cudaGetLastError());
-  return B2_OK;
 }
 
 template <typename T>

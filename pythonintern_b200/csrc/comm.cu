@@ -270,6 +270,8 @@ template <typename T>
 __global__ void __launch_bounds__(512) allreduce_rmsnorm_sharded_kernel(CommView v, int rows, int R, int dim, float* h_slice,
                                                  const float* __restrict__ w, float eps, T* __restrict__ y,
                                                  int64_t timeout_ns, int32_t* status) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   __shared__ int s_ok;
   const uint32_t epoch = v.ctrl[0];
@@ -678,11 +680,11 @@ int b2_allreduce_rmsnorm_sharded(b2_comm* comm, int rows, int dim, int dtype, fl
   int threads = 64;  // one 8-element vector per thread per row up to dim 4096
   while (threads < 512 && threads < dim / 8) threads *= 2;
   if (dtype == B2_BF16)
-    b2::allreduce_rmsnorm_sharded_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
-        v, rows, R, dim, h_slice, norm_w, eps, (__nv_bfloat16*)y, timeout_ns, status);
+    B2_TRY_CUDA(b2::launch_pdl((b2::allreduce_rmsnorm_sharded_kernel<__nv_bfloat16>), dim3(grid), dim3(threads), 0,
+                               stream, v, rows, R, dim, h_slice, norm_w, eps, (__nv_bfloat16*)y, timeout_ns, status));
   else
-    b2::allreduce_rmsnorm_sharded_kernel<float><<<grid, threads, 0, stream>>>(
-        v, rows, R, dim, h_slice, norm_w, eps, (float*)y, timeout_ns, status);
+    B2_TRY_CUDA(b2::launch_pdl((b2::allreduce_rmsnorm_sharded_kernel<float>), dim3(grid), dim3(threads), 0,
+                               stream, v, rows, R, dim, h_slice, norm_w, eps, (float*)y, timeout_ns, status));
   B2_TRY_CUDA(cudaGetLastError());
   return B2_OK;
 }

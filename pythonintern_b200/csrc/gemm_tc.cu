@@ -307,6 +307,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  pdl_wait();  // barrier set-up and TMEM allocation overlap the previous kernel's tail
+  pdl_trigger();
 
   if (warp == 0) {
     // ---------------- TMA producer (one lane)
@@ -592,6 +594,8 @@ __global__ void __launch_bounds__(kThreadsCl, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  pdl_wait();  // barrier set-up and TMEM allocation overlap the previous kernel's tail
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -846,8 +850,7 @@ static int launch(const CUtensorMap& mx, const CUtensorMap& w0, const CUtensorMa
                                      (int)C::SMEM));
     attr_set[dev] = true;
   }
-  gemm_tc_kernel<BN, SWIGLU><<<ctas, kThreads, C::SMEM, s>>>(mx, w0, w1, w2, p);
-  B2_TRY_CUDA(cudaGetLastError());
+  B2_TRY_CUDA(launch_pdl((gemm_tc_kernel<BN, SWIGLU>), dim3(ctas), dim3(kThreads), C::SMEM, s, mx, w0, w1, w2, p));
   return B2_OK;
 }
 
@@ -868,13 +871,15 @@ static int launch_cluster(const CUtensorMap& mx, const CUtensorMap& w0, const CU
   cfg.blockDim = dim3(kThreadsCl, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)p.splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see pdl_wait()
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   B2_TRY_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_cluster_kernel<BN, SWIGLU>, mx, w0, w1, w2, p));
   return B2_OK;
 }

@@ -11,6 +11,8 @@ namespace b2 {
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const void* __restrict__ table,
                                  int vocab, int dim, int dtype, void* __restrict__ out,
                                  int out_dtype, int32_t* status) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   const int64_t id = ids[row];
   const bool ok = id >= 0 && id < vocab;
@@ -29,6 +31,8 @@ __global__ void embedding_kernel(const int64_t* __restrict__ ids, const void* __
 __global__ void rmsnorm_kernel(const void* x, int x_dtype, const void* res, int res_dtype,
                                void* h_out, int h_dtype, const float* __restrict__ w, float eps,
                                void* y, int y_dtype, int dim) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float srow[];
   __shared__ float red[32];
   const size_t base = (size_t)blockIdx.x * dim;
@@ -79,6 +83,8 @@ __device__ __forceinline__ void st8(void* p, int dtype, size_t i, const float (&
 __global__ void rmsnorm_vec_kernel(const void* x, int x_dtype, const void* res, int res_dtype, void* h_out,
                                    int h_dtype, const float* __restrict__ w, float eps, void* y, int y_dtype,
                                    int dim) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   const size_t base = (size_t)blockIdx.x * dim;
   const int nv = dim / 8;
@@ -123,6 +129,8 @@ __global__ void rmsnorm_vec_kernel(const void* x, int x_dtype, const void* res, 
 // First index of the row maximum, like torch.argmax (execution_engine.py:103,133).
 __global__ void argmax_kernel(const float* __restrict__ logits, int64_t ld, int cols,
                               int64_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sv[32];
   __shared__ int si[32];
   const float* row = logits + (size_t)blockIdx.x * ld;
@@ -198,7 +206,8 @@ int b2_embedding(const int64_t* ids, int n, const void* table, int vocab, int di
   B2_CHECK_ARG(b2::valid_dtype(dtype) && b2::valid_dtype(out_dtype), "b2_embedding: bad dtype");
   if (n == 0) return B2_OK;
   B2_CHECK_ARG(ids && table && out, "b2_embedding: null pointer");
-  b2::embedding_kernel<<<n, 256, 0, stream>>>(ids, table, vocab, dim, dtype, out, out_dtype, status);
+  B2_TRY_CUDA(b2::launch_pdl(b2::embedding_kernel, dim3(n), dim3(256), 0, stream, ids, table, vocab, dim, dtype, out,
+                              out_dtype, status));
   B2_TRY_CUDA(cudaGetLastError());
   return B2_OK;
 }
@@ -219,8 +228,8 @@ int b2_rmsnorm(const void* x, int x_dtype, const void* residual, int residual_dt
     int threads = 32;
     while (threads < 256 && threads * 4 < nv) threads *= 2;
     while (threads < nv && threads < 256 && nv / threads > 1) threads *= 2;
-    b2::rmsnorm_vec_kernel<<<rows, threads, 0, stream>>>(x, x_dtype, residual, residual_dtype, h_out, h_dtype,
-                                                          weight, eps, y, y_dtype, dim);
+    B2_TRY_CUDA(b2::launch_pdl(b2::rmsnorm_vec_kernel, dim3(rows), dim3(threads), 0, stream, x, x_dtype, residual,
+                                residual_dtype, h_out, h_dtype, weight, eps, y, y_dtype, dim));
     B2_TRY_CUDA(cudaGetLastError());
     return B2_OK;
   }
@@ -230,8 +239,8 @@ int b2_rmsnorm(const void* x, int x_dtype, const void* residual, int residual_dt
                                      (int)smem));
   }
   const int threads = dim >= 2048 ? 512 : (dim >= 512 ? 256 : 128);
-  b2::rmsnorm_kernel<<<rows, threads, smem, stream>>>(x, x_dtype, residual, residual_dtype, h_out,
-                                                     h_dtype, weight, eps, y, y_dtype, dim);
+  B2_TRY_CUDA(b2::launch_pdl(b2::rmsnorm_kernel, dim3(rows), dim3(threads), smem, stream, x, x_dtype, residual,
+                              residual_dtype, h_out, h_dtype, weight, eps, y, y_dtype, dim));
   B2_TRY_CUDA(cudaGetLastError());
   return B2_OK;
 }
@@ -240,7 +249,7 @@ int b2_argmax(const float* logits, int64_t ld, int rows, int cols, int64_t* out,
   B2_CHECK_ARG(rows >= 0 && cols > 0 && ld >= cols, "b2_argmax: bad sizes");
   if (rows == 0) return B2_OK;
   B2_CHECK_ARG(logits && out, "b2_argmax: null pointer");
-  b2::argmax_kernel<<<rows, 1024, 0, stream>>>(logits, ld, cols, out);
+  B2_TRY_CUDA(b2::launch_pdl(b2::argmax_kernel, dim3(rows), dim3(1024), 0, stream, logits, ld, cols, out));
   B2_TRY_CUDA(cudaGetLastError());
   return B2_OK;
 }

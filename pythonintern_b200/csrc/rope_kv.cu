@@ -48,6 +48,8 @@ __global__ void rope_kv_write_kernel(const T* __restrict__ qkv, int64_t ld_qkv, 
                                      T* __restrict__ q_out, T* __restrict__ k_cache,
                                      T* __restrict__ v_cache, int64_t layer_elems, int layer,
                                      int32_t* status) {
+  pdl_wait();
+  pdl_trigger();
   const int tok = blockIdx.y;
   const int half = hd >> 1;
   const int64_t p = rope_pos[tok];
@@ -133,15 +135,15 @@ extern "C" int b2_rope_kv_write(const void* qkv, int64_t ld_qkv, int n_tokens, i
   const dim3 grid((work + threads - 1) / threads, n_tokens);
   if (dtype == B2_BF16) {
     using T = __nv_bfloat16;
-    b2::rope_kv_write_kernel<T><<<grid, threads, 0, stream>>>(
+    B2_TRY_CUDA(b2::launch_pdl((b2::rope_kv_write_kernel<T>), grid, dim3(threads), 0, stream,
         (const T*)qkv, ld_qkv, nq, nkv, head_dim, rope_pos, store_pos, table_index, block_tables,
         table_stride, num_blocks, block_size, cos, sin, max_seq_len, (T*)q_out, (T*)k_cache,
-        (T*)v_cache, layer_elems, layer, status);
+        (T*)v_cache, layer_elems, layer, status));
   } else {
-    b2::rope_kv_write_kernel<float><<<grid, threads, 0, stream>>>(
+    B2_TRY_CUDA(b2::launch_pdl((b2::rope_kv_write_kernel<float>), grid, dim3(threads), 0, stream,
         (const float*)qkv, ld_qkv, nq, nkv, head_dim, rope_pos, store_pos, table_index,
         block_tables, table_stride, num_blocks, block_size, cos, sin, max_seq_len, (float*)q_out,
-        (float*)k_cache, (float*)v_cache, layer_elems, layer, status);
+        (float*)k_cache, (float*)v_cache, layer_elems, layer, status));
   }
   B2_TRY_CUDA(cudaGetLastError());
   return B2_OK;
