@@ -21,6 +21,9 @@
 // writes silu(g) * u.  Every wait is bounded by %globaltimer; a timeout raises
 // B2_DEV_PIPE_TIMEOUT, drains the copies in flight, frees TMEM and returns.
 #include <cuda.h>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <cudaTypedefs.h>
 
 #include "gemm.cuh"
@@ -790,15 +793,66 @@ struct Plan {
   bool cluster;  // split-K over one thread-block cluster per tile (else the persistent kernel)
 };
 
-// Launch plan.  Measured on B200 over the decode shapes (M = 1..128 tokens; q|k|v,
-// o_proj, gate|up, down of the 8B shape): when the output has at least half as many
-// 128-row tiles as there are SMs, the persistent kernel without split-K streams best;
-// otherwise split K over a thread-block cluster of s CTAs per tile, with the largest s
-// in {8, 4, 2} whose CTAs fit in one wave (clusters of 3, 5 or 6 schedule measurably
-// worse).  The cluster's CTAs exchange float32 partials through an L2 workspace and one
-// cluster barrier, each reducing 1/s of the token columns; an exchange through
-// distributed shared memory measured about twice as slow.  The persistent split-K path
-// (last CTA of a tile reduces) remains for token tiles wider than 128 (BN = 256).
+// Clusters of s CTAs of the split-K kernel that can be resident at once on this device
+// (the GPCs' SM counts decide how clusters of 3, 5, 6 or 7 pack); cached per device.
+template <int BN, bool SWIGLU>
+static int max_active_clusters_t(int s) {
+  using C = Cfg<BN, SWIGLU>;
+  if (cudaFuncSetAttribute(gemm_tc_cluster_kernel<BN, SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)C::SMEM) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)s, 1, 1);
+  cfg.blockDim = dim3(kThreadsCl, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)s;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_cluster_kernel<BN, SWIGLU>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+static int max_active_clusters(int BN, bool swiglu, int s) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const auto key = std::make_tuple(dev, BN, swiglu ? 1 : 0, s);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  switch (BN) {
+    case 16: n = swiglu ? max_active_clusters_t<16, true>(s) : max_active_clusters_t<16, false>(s); break;
+    case 32: n = swiglu ? max_active_clusters_t<32, true>(s) : max_active_clusters_t<32, false>(s); break;
+    case 64: n = swiglu ? max_active_clusters_t<64, true>(s) : max_active_clusters_t<64, false>(s); break;
+    default: n = swiglu ? max_active_clusters_t<128, true>(s) : max_active_clusters_t<128, false>(s); break;
+  }
+  cache[key] = n;
+  return n;
+}
+
+// Launch plan.  When the output has at least half as many 128-row tiles as there are
+// SMs, the persistent kernel without split-K streams best (measured on B200 over the
+// decode shapes: M = 1..128 tokens; q|k|v, o_proj, gate|up, down of the 8B shape).
+// Otherwise K is split over a thread-block cluster of s CTAs per tile, with the largest
+// s <= 8 (the portable cluster size) for which every tile's cluster is resident at once
+// (one wave, asked of the occupancy calculator).  The cluster's CTAs exchange float32
+// partials through an L2 workspace and one cluster barrier, each reducing 1/s of the
+// token columns; an exchange through distributed shared memory, or a barrier built from
+// L2 atomics instead of the cluster barrier, measured about twice as slow.  The
+// persistent split-K path (last CTA of a tile reduces) remains for token tiles wider
+// than 128 (BN = 256).
 static Plan make_plan(int M, int n_tiles, int K, bool swiglu) {
   Plan pl{};
   pl.BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
@@ -810,7 +864,20 @@ static Plan make_plan(int M, int n_tiles, int K, bool swiglu) {
   pl.splits = 1;
   pl.kbps = pl.nkb;
   pl.cluster = false;
-  if (2 * tiles < sms) {
+  if (2 * tiles < sms && BN_FITS_CLUSTER(pl.BN, swiglu)) {
+    const int s_max = (int)std::min<long>(std::min<long>(kMaxClusterSplits, pl.nkb), sms / tiles);
+    for (int s = s_max; s >= 2; --s) {
+      const int kbps = (pl.nkb + s - 1) / s;
+      const int s_eff = (pl.nkb + kbps - 1) / kbps;
+      if (s_eff != s) continue;
+      if (max_active_clusters(pl.BN, swiglu, s) < tiles) continue;
+      pl.splits = s;
+      pl.kbps = kbps;
+      pl.cluster = true;
+      break;
+    }
+  }
+  if (!pl.cluster && 2 * tiles < sms) {
     for (int s : {8, 4, 2}) {
       if (tiles * s > sms || s > pl.nkb) continue;
       const int kbps = (pl.nkb + s - 1) / s;
@@ -818,7 +885,6 @@ static Plan make_plan(int M, int n_tiles, int K, bool swiglu) {
       if (s_eff < 2) continue;
       pl.splits = s_eff;
       pl.kbps = kbps;
-      pl.cluster = BN_FITS_CLUSTER(pl.BN, swiglu) && (s_eff == 2 || s_eff == 4 || s_eff == 8);
       break;
     }
   }
