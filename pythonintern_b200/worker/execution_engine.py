@@ -113,8 +113,9 @@ class WorkerExecutionEngine:
                 top_host = torch.cat(tops).cpu().numpy()
                 self.last_d2h_bytes = tok_host.nbytes + top_host.nbytes
                 _lib.check_device_status(self.device, f"step {step_id}")
-                sampled = [SampledToken(seq_id=sid, token_id=int(tok_host[i]),
-                                        top_logits=[float(x) for x in top_host[i]]) for i, sid in enumerate(ids)]
+                tok_list, top_list = tok_host.tolist(), top_host.tolist()
+                sampled = [SampledToken(seq_id=sid, token_id=tok_list[i], top_logits=top_list[i])
+                           for i, sid in enumerate(ids)]
         self.last_h2d_bytes = h2d
         elapsed_ms = (time.perf_counter() - start) * 1000.0
         self.total_steps_executed += 1

@@ -64,6 +64,11 @@ class DecodeGraph:
                                 table_index=None, tables=self.tables, ctx_lens=self.ctx, max_ctx=width * 16,
                                 compat_pad=not masked_padding)
         self.host = [torch.zeros(total, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+        # Host copy of the packed block tables and the rows they were built from: a
+        # decode step usually changes a few rows (a sequence crossing into a new block),
+        # so only rows that differ from the previous step are converted again.
+        self._tab = np.full((batch, width), -1, dtype=np.int32)
+        self._rows: list = [None] * batch
         self.host_events = [None, None]
         self.host_i = 0
         self.graph: Optional[torch.cuda.CUDAGraph] = None
@@ -80,11 +85,19 @@ class DecodeGraph:
         out[o_tok:o_tok + 8 * B] = np.asarray(tokens, dtype=np.int64).reshape(B).view(np.uint8)
         out[o_pos:o_pos + 8 * B] = pos.view(np.uint8)
         out[o_ctx:o_ctx + 4 * B] = (pos + 1).astype(np.int32).view(np.uint8)
-        tab = np.full((B, W), -1, dtype=np.int32)
+        tab, rows = self._tab, self._rows
+        if len(tables) != B:
+            raise ValueError(f"{len(tables)} block tables for a graph of batch {B}")
         for b, t in enumerate(tables):
-            if len(t) > W:
-                raise ValueError(f"block table of {len(t)} entries exceeds the graph's width {W}")
-            tab[b, :len(t)] = t
+            row = t if isinstance(t, list) else [int(x) for x in t]
+            if rows[b] is not None and row == rows[b]:
+                continue
+            if len(row) > W:
+                raise ValueError(f"block table of {len(row)} entries exceeds the graph's width {W}")
+            row = list(row)
+            tab[b, :len(row)] = row
+            tab[b, len(row):] = -1
+            rows[b] = row
         out[o_tab:o_tab + 4 * B * W] = tab.view(np.uint8).reshape(-1)
         return out
 
