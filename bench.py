@@ -405,9 +405,10 @@ def run_ours(args):
     for name, (fn, nbytes) in gemms.items():
         t = time_fn(fn, 2 * L)
         kern[name] = {"us": t * 1e6, "bytes": nbytes, "gbs": nbytes / t / 1e9}
-    t_lm = time_fn(lambda r=0: kernels.linear(xn, model.lm_head.weight, out_dtype=torch.float32), 4)
-    kern["lm_head"] = {"us": t_lm * 1e6, "bytes": wbytes(model.lm_head.weight),
-                       "gbs": wbytes(model.lm_head.weight) / t_lm / 1e9}
+    v0, v1 = model.vocab_slice()  # TP > 1: this rank's vocabulary rows of the lm_head
+    lm_w = model.lm_head.weight[v0:v1]
+    t_lm = time_fn(lambda r=0: kernels.linear(xn, lm_w, out_dtype=torch.float32), 4)
+    kern["lm_head"] = {"us": t_lm * 1e6, "bytes": wbytes(lm_w), "gbs": wbytes(lm_w) / t_lm / 1e9}
     per_step = {k: v["us"] * (1 if k == "lm_head" else L) for k, v in kern.items()}
     dominant = max(per_step, key=per_step.get)
     peak, peak_kind = measured_peaks()

@@ -222,6 +222,16 @@ int b2_row_parallel_linear(b2_comm* comm, const void* x, int64_t ldx, int M, int
 int b2_allreduce_rmsnorm_sharded(b2_comm* comm, int rows, int dim, int dtype, float* h_slice, const float* norm_w,
                                  float eps, void* y, int64_t timeout_ns, int32_t* status, b2_stream_t stream);
 
+/* Greedy token per row over a vocab-parallel lm_head: replaces torch.argmax over the
+ * replicated logits (execution_engine.py:103,133 on the lm_head of llama.py:168-170).
+ * logits [rows, cols] float32 (row stride ld) are this rank's logits for vocabulary ids
+ * [vocab_offset, vocab_offset + cols); the ranks exchange (max, index) per row through
+ * the communicator and every rank writes the global argmax (first index of the maximum,
+ * NaN wins, as torch.argmax) to out [rows] int64.  rows <= 4096.  Each wait is bounded
+ * by timeout_ns (device bit B2_DEV_PEER_TIMEOUT on expiry). */
+int b2_argmax_allgather(b2_comm* comm, const float* logits, int64_t ld, int rows, int cols, int64_t vocab_offset,
+                        int64_t* out, int64_t timeout_ns, int32_t* status, b2_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,13 +39,15 @@ constexpr int kMaxRanks = 8;
 constexpr int kMaxCtas = 128;
 
 constexpr int kSlots = 3;  // rotating receive slots of the flag-free fused path
+constexpr int kMaxArgRows = 4096;  // rows of one vocab-parallel argmax exchange
 
 struct CommView {
   void* data[2][kMaxRanks];        // every rank's one-shot data buffers (own included)
   void* xn[kSlots][kMaxRanks];     // every rank's all-gather slots of normalised rows
   void* recv_own[kSlots];          // this rank's reduce-scatter receive slots
   uint32_t* flags[kMaxRanks];      // every rank's flag array [kMaxRanks][kMaxCtas]
-  uint32_t* ctrl;                  // own {epoch, done}
+  char* amx[kMaxRanks];             // every rank's argmax exchange slots [kSlots][kMaxRanks][kMaxArgRows]
+  uint32_t* ctrl;                  // own control words (epochs, done counters, slot extents)
   size_t slot_bytes;
   int rank, world;
 };
@@ -55,7 +57,7 @@ struct CommView {
 struct b2_comm {
   int rank, world, device;
   size_t max_bytes, data_bytes;
-  size_t off_data[2], off_recv[b2::kSlots], off_xn[b2::kSlots], off_flags, off_ctrl, off_table, total;
+  size_t off_data[2], off_recv[b2::kSlots], off_xn[b2::kSlots], off_flags, off_ctrl, off_table, off_amx, total;
   unsigned long long* scatter_table;  // device: [kSlots][kMaxRanks] every rank's receive slot addresses
   char* base;                       // own allocation
   char* peer_base[b2::kMaxRanks];   // mapped peers (own base at [rank])
@@ -401,6 +403,79 @@ __global__ void __launch_bounds__(512) allreduce_rmsnorm_sharded_kernel(CommView
   comm_finish(v);
 }
 
+// Greedy token over a vocab-parallel lm_head (the replicated-logits argmax of
+// execution_engine.py:103,133).  CTA per row: the block argmax over this rank's vocab
+// slice, then thread 0 stores (value bits << 32 | global index) into slot b of every
+// rank's exchange buffer and waits (sentinel polling, bounded) for the world's entries of
+// its row, taking the best in rank order: rank order is vocab order, so a tie keeps the
+// smaller index and the first NaN wins, exactly as an argmax over the full row.  The slot
+// of the previous call is re-armed; the last CTA advances the exchange epoch (ctrl[8]).
+__global__ void __launch_bounds__(1024) argmax_allgather_kernel(CommView v, const float* __restrict__ logits,
+                                                                int64_t ld, int rows, int cols, int64_t vocab_offset,
+                                                                int64_t* __restrict__ out, int64_t timeout_ns,
+                                                                int32_t* status) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const uint32_t epoch = v.ctrl[8];
+  const int b = (int)(epoch % kSlots);
+  const int prev = (b + kSlots - 1) % kSlots;
+  if (blockIdx.x == 0 && threadIdx.x == 0) v.ctrl[10 + b] = (uint32_t)rows;
+  float best;
+  int bi;
+  block_argmax(logits + (size_t)blockIdx.x * ld, cols, sv, si, best, bi);
+  if (threadIdx.x == 0) {
+    const uint32_t gidx = (uint32_t)(vocab_offset + (bi == 0x7fffffff ? 0 : bi));
+    const unsigned long long packed = ((unsigned long long)__float_as_uint(best) << 32) | gidx;
+    for (int q = 0; q < v.world; ++q) {
+      unsigned long long* dst = reinterpret_cast<unsigned long long*>(v.amx[q]) +
+                                ((size_t)(b * kMaxRanks + v.rank) * kMaxArgRows + blockIdx.x);
+      *reinterpret_cast<volatile unsigned long long*>(dst) = packed;
+    }
+    const uint64_t deadline = globaltimer_ns() + (uint64_t)timeout_ns;
+    const unsigned long long* own = reinterpret_cast<const unsigned long long*>(v.amx[v.rank]);
+    float bv = 0.f;
+    uint32_t bidx = 0;
+    bool ok = true;
+    for (int src = 0; src < v.world && ok; ++src) {
+      const volatile unsigned long long* p = own + ((size_t)(b * kMaxRanks + src) * kMaxArgRows + blockIdx.x);
+      unsigned long long x = *p;
+      uint32_t it = 0;
+      while (x == ~0ull) {
+        if ((++it & 63) == 0 && globaltimer_ns() > deadline) {
+          ok = false;
+          break;
+        }
+        x = *p;
+      }
+      if (!ok) break;
+      const float xv = __uint_as_float((uint32_t)(x >> 32));
+      if (src == 0 || xv > bv || (xv != xv && bv == bv)) {
+        bv = xv;
+        bidx = (uint32_t)x;
+      }
+    }
+    if (!ok) raise_status(status, B2_DEV_PEER_TIMEOUT);
+    out[blockIdx.x] = (int64_t)bidx;
+  }
+  // Re-arm this rank's slot of the previous call, over the rows that call used.
+  const int prow = (int)v.ctrl[10 + prev];
+  unsigned long long* own_prev = reinterpret_cast<unsigned long long*>(v.amx[v.rank]) + (size_t)prev * kMaxRanks * kMaxArgRows;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < v.world * prow; i += gridDim.x * blockDim.x)
+    own_prev[(size_t)(i / prow) * kMaxArgRows + (i % prow)] = ~0ull;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t d = atomicAdd(v.ctrl + 9, 1u);
+    if (d == gridDim.x - 1) {
+      v.ctrl[9] = 0;
+      v.ctrl[8] = epoch + 1;
+      __threadfence();
+    }
+  }
+}
+
 static CommView make_view(const b2_comm* c) {
   CommView v{};
   v.rank = c->rank;
@@ -410,6 +485,7 @@ static CommView make_view(const b2_comm* c) {
     v.data[1][r] = c->peer_base[r] + c->off_data[1];
     for (int k = 0; k < kSlots; ++k) v.xn[k][r] = c->peer_base[r] + c->off_xn[k];
     v.flags[r] = reinterpret_cast<uint32_t*>(c->peer_base[r] + c->off_flags);
+    v.amx[r] = c->peer_base[r] + c->off_amx;
   }
   for (int k = 0; k < kSlots; ++k) v.recv_own[k] = c->base + c->off_recv[k];
   v.slot_bytes = c->data_bytes;
@@ -461,13 +537,15 @@ int b2_comm_create(int rank, int world_size, size_t max_bytes, b2_comm** out) {
   c->off_flags = (2 + 2 * b2::kSlots) * c->data_bytes;
   c->off_ctrl = c->off_flags + b2::align_up((size_t)b2::kMaxRanks * b2::kMaxCtas * sizeof(uint32_t), 256);
   c->off_table = c->off_ctrl + 256;
-  c->total = c->off_table + 256;
+  c->off_amx = c->off_table + 256;
+  c->total = c->off_amx + (size_t)b2::kSlots * b2::kMaxRanks * b2::kMaxArgRows * sizeof(uint64_t);
   cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&c->base), c->total);
   if (e != cudaSuccess) {
     delete c;
     return b2::fail(B2_ECUDA, "b2_comm_create: cudaMalloc(%zu): %s", (size_t)0, cudaGetErrorString(e));
   }
-  e = cudaMemset(c->base + c->off_flags, 0, c->total - c->off_flags);
+  e = cudaMemset(c->base + c->off_flags, 0, c->off_amx - c->off_flags);
+  if (e == cudaSuccess) e = cudaMemset(c->base + c->off_amx, 0xff, c->total - c->off_amx);
   if (e == cudaSuccess) e = cudaMemset(c->base, 0, 2 * c->data_bytes);
   // idle receive and all-gather slots hold the sentinel
   if (e == cudaSuccess) e = cudaMemset(c->base + c->off_recv[0], 0xff, 2 * b2::kSlots * c->data_bytes);
@@ -658,6 +736,20 @@ int b2_row_parallel_linear(b2_comm* comm, const void* x, int64_t ldx, int M, int
   b2::GemmSeg seg{w, N, 0};
   return b2::gemm_tc(x, ldx, M, K, &seg, 1, b2::kEpiStore, nullptr, nullptr, N, dtype, workspace, workspace_bytes,
                      status, stream, &sc);
+}
+
+int b2_argmax_allgather(b2_comm* comm, const float* logits, int64_t ld, int rows, int cols, int64_t vocab_offset,
+                        int64_t* out, int64_t timeout_ns, int32_t* status, b2_stream_t stream) {
+  B2_CHECK_ARG(comm && comm->opened, "b2_argmax_allgather: communicator not opened");
+  B2_CHECK_ARG(rows >= 0 && rows <= b2::kMaxArgRows, "b2_argmax_allgather: %d rows (at most %d)", rows, b2::kMaxArgRows);
+  B2_CHECK_ARG(cols > 0 && ld >= cols && vocab_offset >= 0 && vocab_offset + cols < (int64_t)0x7fffffff,
+               "b2_argmax_allgather: bad sizes cols=%d ld=%lld offset=%lld", cols, (long long)ld, (long long)vocab_offset);
+  if (rows == 0) return B2_OK;
+  B2_CHECK_ARG(logits && out, "b2_argmax_allgather: null pointer");
+  const b2::CommView v = b2::make_view(comm);
+  B2_TRY_CUDA(b2::launch_pdl(b2::argmax_allgather_kernel, dim3(rows), dim3(1024), 0, stream, v, logits, ld, rows,
+                             cols, vocab_offset, out, timeout_ns, status));
+  return B2_OK;
 }
 
 int b2_allreduce_rmsnorm_sharded(b2_comm* comm, int rows, int dim, int dtype, float* h_slice, const float* norm_w,

@@ -118,6 +118,69 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// First index of the maximum of row[0, cols) over the whole CTA (blockDim a multiple of
+// 32, at most 1024), like torch.argmax: ties go to the smaller index and NaN beats any
+// number.  The result is valid in thread 0 (best value, index; index 0x7fffffff for an
+// empty row).  sv/si: shared scratch of 32 entries each.
+__device__ __forceinline__ bool argmax_better(float v, int c, float best, int bi) {
+  return v > best || (v == best && c < bi) || (v != v && best == best);
+}
+__device__ __forceinline__ void block_argmax(const float* row, int cols, float* sv, int* si, float& best, int& bi) {
+  best = -INFINITY;
+  bi = 0x7fffffff;
+  auto take = [&](float v, int c) {
+    if (argmax_better(v, c, best, bi)) {
+      best = v;
+      bi = c;
+    }
+  };
+  if ((((uintptr_t)row) & 15) == 0) {
+    const int n4 = cols / 4;
+    const float4* row4 = reinterpret_cast<const float4*>(row);
+    int c4 = threadIdx.x;
+    for (; c4 + 3 * (int)blockDim.x < n4; c4 += 4 * blockDim.x) {  // four 16-byte loads in flight
+      float4 a[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = __ldg(row4 + c4 + u * blockDim.x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = 4 * (c4 + u * blockDim.x);
+        take(a[u].x, c); take(a[u].y, c + 1); take(a[u].z, c + 2); take(a[u].w, c + 3);
+      }
+    }
+    for (; c4 < n4; c4 += blockDim.x) {
+      const float4 a = __ldg(row4 + c4);
+      take(a.x, 4 * c4); take(a.y, 4 * c4 + 1); take(a.z, 4 * c4 + 2); take(a.w, 4 * c4 + 3);
+    }
+    for (int c = 4 * n4 + threadIdx.x; c < cols; c += blockDim.x) take(row[c], c);
+  } else {
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) take(row[c], c);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    take(ov, oi);
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    sv[warp] = best;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      take(ov, oi);
+    }
+  }
+}
+
 // Programmatic dependent launch.  Kernels of the decode step are launched with
 // programmatic stream serialization (launch_pdl), so the next kernel in the stream can be
 // scheduled while the current one drains.  Every such kernel calls pdl_wait() before it

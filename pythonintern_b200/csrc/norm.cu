@@ -133,67 +133,10 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int64_t ld, int 
   pdl_trigger();
   __shared__ float sv[32];
   __shared__ int si[32];
-  const float* row = logits + (size_t)blockIdx.x * ld;
-  float best = -INFINITY;
-  int bi = 0x7fffffff;
-  auto take = [&](float v, int c) {
-    if (v > best || (v == best && c < bi) || (v != v && best == best)) {  // NaN wins, like torch
-      best = v;
-      bi = c;
-    }
-  };
-  if ((((uintptr_t)row) & 15) == 0) {
-    const int n4 = cols / 4;
-    const float4* row4 = reinterpret_cast<const float4*>(row);
-    int c4 = threadIdx.x;
-    for (; c4 + 3 * (int)blockDim.x < n4; c4 += 4 * blockDim.x) {  // four 16-byte loads in flight
-      float4 a[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) a[u] = __ldg(row4 + c4 + u * blockDim.x);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int c = 4 * (c4 + u * blockDim.x);
-        take(a[u].x, c); take(a[u].y, c + 1); take(a[u].z, c + 2); take(a[u].w, c + 3);
-      }
-    }
-    for (; c4 < n4; c4 += blockDim.x) {
-      const float4 a = __ldg(row4 + c4);
-      take(a.x, 4 * c4); take(a.y, 4 * c4 + 1); take(a.z, 4 * c4 + 2); take(a.w, 4 * c4 + 3);
-    }
-    for (int c = 4 * n4 + threadIdx.x; c < cols; c += blockDim.x) take(row[c], c);
-  } else {
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) take(row[c], c);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > best || (ov == best && oi < bi) || (ov != ov && best == best)) {
-      best = ov;
-      bi = oi;
-    }
-  }
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) {
-    sv[warp] = best;
-    si[warp] = bi;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    const int nw = blockDim.x >> 5;
-    best = lane < nw ? sv[lane] : -INFINITY;
-    bi = lane < nw ? si[lane] : 0x7fffffff;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > best || (ov == best && oi < bi) || (ov != ov && best == best)) {
-        best = ov;
-        bi = oi;
-      }
-    }
-    if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
-  }
+  float best;
+  int bi;
+  block_argmax(logits + (size_t)blockIdx.x * ld, cols, sv, si, best, bi);
+  if (threadIdx.x == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
 }
 
 }  // namespace b2

@@ -179,6 +179,45 @@ class DistributedLLaMAModel(nn.Module):
                 trace.append(h.clone())
         return xn
 
+    def vocab_slice(self):
+        """Vocabulary ids [start, end) whose logits this rank computes in ``greedy``.
+
+        The lm_head weight stays replicated (llama.py:121; sharding.py:105-107), so
+        checkpoints load unchanged; with world_size > 1 each rank multiplies only its
+        contiguous row slice of it and the ranks exchange one (max, index) pair per row.
+        """
+        V, t = self.config.vocab_size, max(1, self.world_size)
+        per = -(-V // t)
+        start = min(V, self.rank * per)
+        return start, min(V, start + per)
+
+    def greedy(self, token_ids: torch.Tensor, positions: Optional[torch.Tensor],
+               kv_pool: PhysicalKVCachePool, block_tables: Optional[List[List[int]]], is_prefill: bool = False,
+               step_id: int = 0, metadata: Optional[TokenMetadata] = None):
+        """Greedy next token and the first ten logits of each sequence's last position.
+
+        Equals ``argmax(forward(...))`` and ``forward(...)[:, :10]`` (execution_engine.py:
+        103-108, 131-135) without materialising the full logits on every rank.
+        """
+        with torch.no_grad():
+            B, S = token_ids.shape
+            md = metadata or build_metadata(positions, block_tables, is_prefill, self.device,
+                                            masked_padding=self.config.masked_decode_padding)
+            xn = self.forward_hidden(token_ids, md, kv_pool)
+            last = xn.view(B, S, -1)[:, -1, :]  # row-strided view, no copy
+            w = self.lm_head.weight
+            if self.world_size == 1:
+                logits = kernels.linear(last, w, out_dtype=torch.float32)
+                return kernels.argmax(logits), logits[:, :10]
+            v0, v1 = self.vocab_slice()
+            logits = kernels.linear(last, w[v0:v1], out_dtype=torch.float32)
+            tok = self.communicator.argmax_allgather(logits, v0)
+            if v0 == 0 and v1 >= 10:
+                top = logits[:, :10]
+            else:
+                top = kernels.linear(last, w[:10], out_dtype=torch.float32)
+            return tok, top
+
     def forward(self, token_ids: torch.Tensor, positions: torch.Tensor,
                 kv_pool: Optional[PhysicalKVCachePool] = None, block_tables: Optional[List[List[int]]] = None,
                 is_prefill: bool = True, step_id: int = 0, return_logits_last_only: bool = True,

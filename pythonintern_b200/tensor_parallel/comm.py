@@ -261,6 +261,26 @@ class DistributedCommunicator:
               "b2_allreduce_rmsnorm_sharded")
         return out
 
+    def argmax_allgather(self, logits: torch.Tensor, vocab_offset: int, out: Optional[torch.Tensor] = None,
+                         timeout_sec: float = 15.0) -> torch.Tensor:
+        """Greedy token per row when each rank holds the logits of one vocabulary slice.
+
+        ``logits`` [rows, cols] float32 are this rank's logits for ids
+        [vocab_offset, vocab_offset + cols); returns the global argmax [rows] int64 on every
+        rank, equal to torch.argmax over the full row (execution_engine.py:103,133).
+        """
+        self._require_open()
+        _lib.require_cuda(logits, "logits")
+        if logits.dtype != torch.float32 or logits.dim() != 2 or logits.stride(1) != 1:
+            raise ValueError("argmax_allgather: logits must be a row-major [rows, cols] float32 tensor")
+        rows, cols = logits.shape
+        if out is None:
+            out = torch.empty(rows, dtype=torch.int64, device=self.device)
+        check(_lib.lib().b2_argmax_allgather(self._comm, ptr(logits), logits.stride(0), rows, cols, int(vocab_offset),
+                                             ptr(out), int(timeout_sec * 1e9), status_ptr(self.device),
+                                             stream_ptr(self.device)), "b2_argmax_allgather")
+        return out
+
     def cleanup(self):
         """Release the symmetric buffers and peer mappings (comm.py:156-166)."""
         self._views.clear()

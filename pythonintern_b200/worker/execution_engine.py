@@ -20,7 +20,7 @@ from typing import List, Optional
 import numpy as np
 import torch
 
-from pythonintern_b200 import _lib, kernels
+from pythonintern_b200 import _lib
 from pythonintern_b200.config import KVCacheConfig, ModelConfig, ShardConfig
 from pythonintern_b200.model.kv_cache import KVCacheManager
 from pythonintern_b200.model.llama import DistributedLLaMAModel
@@ -56,11 +56,6 @@ class WorkerExecutionEngine:
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
 
-    def _sample(self, logits: torch.Tensor):
-        """Greedy token per row on the device, plus the first ten logits (execution_engine.py:103-108)."""
-        tok = kernels.argmax(logits)
-        return tok, logits[:, :10]
-
     def execute_step(self, step_request) -> StepResponse:
         start = time.perf_counter()
         step_id = step_request.step_id
@@ -79,8 +74,7 @@ class WorkerExecutionEngine:
                 md = build_metadata(np.arange(P, dtype=np.int64)[None, :], table, True, self.device,
                                     stager=self.stager, extra=prompt)
                 h2d += self.stager.last_bytes
-                logits = self.model(md.extra, None, pool, table, True, step_id, True, metadata=md)
-                t, tl = self._sample(logits)
+                t, tl = self.model.greedy(md.extra, None, pool, table, True, step_id, metadata=md)
                 toks.append(t)
                 tops.append(tl)
                 ids.append(slot.seq_id)
@@ -95,15 +89,13 @@ class WorkerExecutionEngine:
                     h2d += g.nbytes
                     if new:
                         g.capture()
-                    t, logits = g.replay()
-                    tl = logits[:, :10]
+                    t, tl = g.replay()
                 else:
                     md = build_metadata(pos, tables, False, self.device,
                                         masked_padding=self.model_config.masked_decode_padding,
                                         stager=self.stager, extra=tok_ids)
                     h2d += self.stager.last_bytes
-                    logits = self.model(md.extra, None, pool, tables, False, step_id, True, metadata=md)
-                    t, tl = self._sample(logits)
+                    t, tl = self.model.greedy(md.extra, None, pool, tables, False, step_id, metadata=md)
                 toks.append(t)
                 tops.append(tl)
                 ids.extend(s.seq_id for s in decode_slots)

@@ -23,7 +23,6 @@ from typing import Dict, Optional, Sequence, Tuple
 import numpy as np
 import torch
 
-from pythonintern_b200 import kernels
 from pythonintern_b200.model.metadata import TokenMetadata
 
 
@@ -72,7 +71,7 @@ class DecodeGraph:
         self.host_events = [None, None]
         self.host_i = 0
         self.graph: Optional[torch.cuda.CUDAGraph] = None
-        self.logits: Optional[torch.Tensor] = None
+        self.top: Optional[torch.Tensor] = None
         self.next_tok: Optional[torch.Tensor] = None
 
     # -- packing -------------------------------------------------------------------
@@ -115,8 +114,7 @@ class DecodeGraph:
 
     # -- capture / replay -------------------------------------------------------------
     def _step(self):
-        logits = self.model(self.tok, None, self.pool, [[]] * self.batch, False, 0, True, metadata=self.md)
-        return logits, kernels.argmax(logits)
+        return self.model.greedy(self.tok, None, self.pool, [[]] * self.batch, False, 0, metadata=self.md)
 
     def capture(self):
         """Runs the step once eagerly (sizes workspaces, sets kernel attributes), then captures it.
@@ -129,12 +127,13 @@ class DecodeGraph:
             torch.cuda.synchronize(self.device)
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self.logits, self.next_tok = self._step()
+                self.next_tok, self.top = self._step()
         self.graph = g
 
     def replay(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Runs the captured step; returns (greedy tokens [batch], first ten logits [batch, 10])."""
         self.graph.replay()
-        return self.next_tok, self.logits
+        return self.next_tok, self.top
 
 
 class DecodeGraphCache:

@@ -2,6 +2,7 @@
 
 * The reference's in-memory all-reduce tests (tests/test_tensor_parallel.py:61-118,
   tests/test_grpc_collectives.py:11-43) with one thread per GPU.
+* The vocab-parallel greedy token exchange against torch.argmax over the full row.
 * The Tiny LLaMA workload at TP=2 with one process per GPU: greedy tokens identical to
   the reference's TP=2 run.
 * A Llama-3-8B-shape bf16 layer at TP=2 against the oracle.
@@ -90,6 +91,41 @@ def test_all_reduce_4_ranks():
     [t.join() for t in th]
     for r in range(4):
         assert torch.equal(res[r], torch.full((2, 8), 10.0))
+    for c in comms:
+        c.cleanup()
+
+
+@pytest.mark.skipif(NGPU < 2, reason="needs 2 GPUs")
+def test_vocab_parallel_argmax_matches_full_argmax():
+    """Each rank holds one vocab slice of the logits; the exchanged greedy token equals
+    torch.argmax over the full row, ties across the slice boundary and NaN included,
+    on several calls in a row (the exchange slots rotate)."""
+    from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
+    comms = [DistributedCommunicator(rank=r, world_size=2, device=f"cuda:{r}") for r in range(2)]
+    comms[0].register_in_memory_peer(1, comms[1])
+    comms[1].register_in_memory_peer(0, comms[0])
+    V, rows = 1001, 37
+    half = (V + 1) // 2
+    gen = torch.Generator().manual_seed(3)
+    for call in range(4):
+        full = torch.randn(rows, V, generator=gen)
+        full[0, 10] = full[0, half + 5] = 50.0       # tie across the boundary: the smaller index wins
+        full[1, half + 7] = 60.0                       # maximum in the second slice
+        full[2, 3] = full[2, 4] = 70.0                 # tie inside the first slice
+        full[3, half + 1] = float("nan")               # NaN wins, like torch.argmax
+        expected = torch.argmax(full, dim=1)
+        res = [None, None]
+
+        def run(r):
+            with torch.cuda.device(r):
+                v0, v1 = (0, half) if r == 0 else (half, V)
+                sl = full[:, v0:v1].contiguous().to(f"cuda:{r}")
+                res[r] = comms[r].argmax_allgather(sl, v0).cpu()
+        th = [threading.Thread(target=run, args=(r,)) for r in range(2)]
+        [t.start() for t in th]
+        [t.join() for t in th]
+        for r in range(2):
+            assert torch.equal(res[r], expected), (call, r)
     for c in comms:
         c.cleanup()
 
