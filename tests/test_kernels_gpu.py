@@ -106,6 +106,7 @@ def test_linear_float32(M, N, K):
 @pytest.mark.parametrize("M,N,K", [
     (1, 128, 64), (1, 4096, 4096), (7, 384, 512), (16, 256, 2048), (33, 1024, 1024), (64, 512, 5632),
     (128, 6144, 4096), (129, 256, 256), (200, 384, 320), (300, 640, 2048), (1, 4096, 14336),
+    (128, 14336, 4096), (100, 12800, 1024), (64, 10240, 2048),  # 74..147 tiles: one wave, idle SMs
 ])
 def test_linear_bf16_tensor_cores(M, N, K):
     """tcgen05 GEMM (swap-AB, split-K where chosen) against the float64 oracle on the same bf16 inputs."""
@@ -149,7 +150,8 @@ def test_linear_qkv(dtype, M):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("M,N,K", [(1, 344, 256), (8, 2816, 2048), (128, 1792, 4096), (70, 200, 256)])
+@pytest.mark.parametrize("M,N,K", [(1, 344, 256), (8, 2816, 2048), (128, 1792, 4096), (70, 200, 256),
+                                   (128, 14336, 4096), (16, 12288, 1024)])
 def test_linear_swiglu(dtype, M, N, K):
     x = torch.randn(M, K, generator=g(M)).to(DEV, dtype)
     wg = (torch.randn(N, K, generator=g(1)) / math.sqrt(K)).to(DEV, dtype)
@@ -158,6 +160,23 @@ def test_linear_swiglu(dtype, M, N, K):
     xn = to_np(x)
     want = oracle.silu(xn @ to_np(wg).T) * (xn @ to_np(wu).T)
     assert rel(to_np(y), want) < (1e-5 if dtype == torch.float32 else 8e-3)
+
+
+def test_large_gemm_repeated_calls_are_identical():
+    """The 8B gate|up shape (112 tiles) and a plain GEMM over the same weight, called back
+    to back and interleaved: results agree bit for bit between calls."""
+    M, N, K = 128, 14336, 4096
+    x = torch.randn(M, K, generator=g(7)).to(DEV, torch.bfloat16)
+    wg = (torch.randn(N, K, generator=g(8)) / math.sqrt(K)).to(DEV, torch.bfloat16)
+    wu = (torch.randn(N, K, generator=g(9)) / math.sqrt(K)).to(DEV, torch.bfloat16)
+    y1 = kernels.linear_swiglu(x, wg, wu)
+    y2 = kernels.linear(x, wg)
+    y3 = kernels.linear_swiglu(x, wg, wu)
+    y4 = kernels.linear(x, wg)
+    torch.cuda.synchronize()
+    _lib.check_device_status(DEV, "large GEMM")
+    assert torch.equal(y1, y3) and torch.equal(y2, y4)
+    assert rel(to_np(y2), to_np(x) @ to_np(wg).T) < 8e-3
 
 
 def test_split_k_workspace_shared_across_shapes():
