@@ -201,14 +201,20 @@ def status_ptr(device) -> int:
     return device_state(device).status.data_ptr()
 
 
+def raise_for_status(v: int, what: str = "kernel"):
+    """Raises the exception a kernel error word stands for (nothing when it is 0)."""
+    if v:
+        if v & B2_DEV_PEER_TIMEOUT:
+            raise TimeoutError(f"{what}: a tensor-parallel peer did not arrive before the all-reduce timeout")
+        if v & B2_DEV_RANGE:
+            raise IndexError(f"{what}: position, block-table entry or token id out of range")
+        raise B2Error(f"{what}: device error bits {v:#x}")
+
+
 def check_device_status(device, what: str = "kernel"):
     """Synchronise the device, read and clear the kernel error word, raise on error."""
     st = device_state(device)
     v = int(st.status.item())
     if v:
         st.status.zero_()
-        if v & B2_DEV_PEER_TIMEOUT:
-            raise TimeoutError(f"{what}: a tensor-parallel peer did not arrive before the all-reduce timeout")
-        if v & B2_DEV_RANGE:
-            raise IndexError(f"{what}: position, block-table entry or token id out of range")
-        raise B2Error(f"{what}: device error bits {v:#x}")
+        raise_for_status(v, what)

@@ -51,10 +51,36 @@ class WorkerExecutionEngine:
         self.stager = PinnedStager(dev)
         self.use_cuda_graphs = use_cuda_graphs
         self.graphs = DecodeGraphCache(self.model, self.kv_manager.pool, model_config.masked_decode_padding)
+        self._pin_tok: Optional[torch.Tensor] = None  # pinned read-back buffers (_read_back)
+        self._pin_top: Optional[torch.Tensor] = None
+        self._pin_status = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self.total_steps_executed = 0
         self.total_latency_ms = 0.0
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
+
+    def _read_back(self, toks: List[torch.Tensor], tops: List[torch.Tensor], step_id: int):
+        """Sampled tokens, first ten logits and the kernels' error word in one synchronisation.
+
+        Asynchronous copies into pinned host buffers, then one stream synchronise; a set
+        error word is cleared and raised after the wait.
+        """
+        tok = toks[0] if len(toks) == 1 else torch.cat(toks)
+        top = tops[0] if len(tops) == 1 else torch.cat(tops)
+        n = tok.shape[0]
+        if self._pin_tok is None or self._pin_tok.shape[0] < n:
+            self._pin_tok = torch.empty(n, dtype=torch.int64, pin_memory=True)
+            self._pin_top = torch.empty(n, 10, dtype=torch.float32, pin_memory=True)
+        st = _lib.device_state(self.device).status
+        self._pin_tok[:n].copy_(tok, non_blocking=True)
+        self._pin_top[:n].copy_(top, non_blocking=True)
+        self._pin_status.copy_(st, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        v = int(self._pin_status[0])
+        if v:
+            st.zero_()
+            _lib.raise_for_status(v, f"step {step_id}")
+        return self._pin_tok[:n].numpy(), self._pin_top[:n].numpy()
 
     def execute_step(self, step_request) -> StepResponse:
         start = time.perf_counter()
@@ -81,8 +107,8 @@ class WorkerExecutionEngine:
             if decode_slots:
                 tok_ids = np.asarray([[s.current_token_id] for s in decode_slots], dtype=np.int64)
                 pos = np.asarray([[s.current_len - 1] for s in decode_slots], dtype=np.int64)
-                tables = [list(s.block_table) for s in decode_slots]
                 if self.use_cuda_graphs:
+                    tables = [s.block_table for s in decode_slots]  # packed row by row, only where changed
                     # One graph replay per step (worker/graphs.py); captured on first use.
                     g, new = self.graphs.get(len(decode_slots), max(len(t) for t in tables))
                     g.upload_host(tok_ids.reshape(-1), pos.reshape(-1), tables)
@@ -91,6 +117,7 @@ class WorkerExecutionEngine:
                         g.capture()
                     t, tl = g.replay()
                 else:
+                    tables = [list(s.block_table) for s in decode_slots]
                     md = build_metadata(pos, tables, False, self.device,
                                         masked_padding=self.model_config.masked_decode_padding,
                                         stager=self.stager, extra=tok_ids)
@@ -101,10 +128,8 @@ class WorkerExecutionEngine:
                 ids.extend(s.seq_id for s in decode_slots)
             sampled = []
             if toks:
-                tok_host = torch.cat(toks).cpu().numpy()
-                top_host = torch.cat(tops).cpu().numpy()
+                tok_host, top_host = self._read_back(toks, tops, step_id)
                 self.last_d2h_bytes = tok_host.nbytes + top_host.nbytes
-                _lib.check_device_status(self.device, f"step {step_id}")
                 tok_list, top_list = tok_host.tolist(), top_host.tolist()
                 sampled = [SampledToken(seq_id=sid, token_id=tok_list[i], top_logits=top_list[i])
                            for i, sid in enumerate(ids)]
