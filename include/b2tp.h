@@ -98,6 +98,28 @@ int b2_linear_swiglu(const void* x, int64_t ldx, int M, int K, const void* w_gat
                      int N, void* y, int64_t ldy, int dtype, void* workspace,
                      size_t workspace_bytes, int32_t* status, b2_stream_t stream);
 
+/* Deferred RMSNorm at world size 1 (bf16, M <= 128 rows).  Together these replace
+ * RowParallelLinear.forward + the residual add + the next RMSNorm (layers.py:147-162,
+ * 179-184; llama.py:70-75) followed by the next ColumnParallelLinear / SwiGLU
+ * (attention.py:156-158, mlp.py:80-82), without a separate normalisation kernel:
+ *   b2_linear_residual_norm: h [M, N] float32 (row stride ldh) += x @ w^T, then
+ *     z [M, N] bf16 = h * norm_w (not yet divided by the RMS) and ss [M, N/128] = the
+ *     sum of h^2 over each 128-column tile.  N % 128 == 0.  Returns B2_ENOTSUP, before
+ *     launching anything, when the shape gets no split-K cluster plan (the caller then
+ *     uses b2_linear + b2_rmsnorm).  Workspace: b2_linear_workspace_bytes(M, N, K).
+ *   b2_linear_qkv_rownorm / b2_linear_swiglu_rownorm: b2_linear_qkv / b2_linear_swiglu on
+ *     x = z whose output row m is scaled by rsqrt(sum_j ss[m * n_ss + j] / dim + eps),
+ *     i.e. the GEMM of the normalised rows (the two SwiGLU halves both scaled). */
+int b2_linear_residual_norm(const void* x, int64_t ldx, int M, int K, const void* w, int N, float* h, int64_t ldh,
+                            const float* norm_w, void* z, int64_t ldz, float* ss, void* workspace,
+                            size_t workspace_bytes, int32_t* status, b2_stream_t stream);
+int b2_linear_qkv_rownorm(const void* x, int64_t ldx, int M, int K, const void* wq, int Nq, const void* wk, int Nk,
+                          const void* wv, int Nv, void* y, int64_t ldy, const float* ss, int n_ss, int dim, float eps,
+                          void* workspace, size_t workspace_bytes, int32_t* status, b2_stream_t stream);
+int b2_linear_swiglu_rownorm(const void* x, int64_t ldx, int M, int K, const void* w_gate, const void* w_up, int N,
+                             void* y, int64_t ldy, const float* ss, int n_ss, int dim, float eps, void* workspace,
+                             size_t workspace_bytes, int32_t* status, b2_stream_t stream);
+
 /* ---------------------------------------------------------------- RoPE + paged KV write
  * For token i (0 <= i < n_tokens) with row = table_index ? table_index[i] : i:
  *   q_out[i, h, :]   = rope(qkv[i, q-head h], rope_pos[i])                 (attention.py:46-63,161)

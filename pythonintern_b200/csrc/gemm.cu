@@ -73,4 +73,64 @@ int b2_linear_swiglu(const void* x, int64_t ldx, int M, int K, const void* w_gat
                      status, stream);
 }
 
+int b2_linear_residual_norm(const void* x, int64_t ldx, int M, int K, const void* w, int N, float* h, int64_t ldh,
+                            const float* norm_w, void* z, int64_t ldz, float* ss, void* workspace,
+                            size_t workspace_bytes, int32_t* status, b2_stream_t stream) {
+  int rc = b2::check_common(x, M, K, N, B2_BF16, B2_BF16, "b2_linear_residual_norm");
+  if (rc) return rc;
+  B2_CHECK_ARG(ldx >= K && ldh >= N && ldz >= N, "b2_linear_residual_norm: row strides too small");
+  if (M == 0) return B2_OK;
+  B2_CHECK_ARG(w && h && norm_w && z && ss, "b2_linear_residual_norm: null pointer");
+  if (M > 128 || N % 128 != 0)
+    return b2::fail(B2_ENOTSUP, "b2_linear_residual_norm: needs M <= 128 and N %% 128 == 0 (M=%d N=%d)", M, N);
+  b2::GemmSeg seg{w, N, 0};
+  b2::RowNorm rn{};
+  rn.res_h = h;
+  rn.ldh = ldh;
+  rn.norm_w = norm_w;
+  rn.z = z;
+  rn.ldz = ldz;
+  rn.ss_out = ss;
+  return b2::gemm_tc(x, ldx, M, K, &seg, 1, b2::kEpiStore, nullptr, nullptr, N, B2_BF16, workspace, workspace_bytes,
+                     status, stream, nullptr, &rn);
+}
+
+int b2_linear_qkv_rownorm(const void* x, int64_t ldx, int M, int K, const void* wq, int Nq, const void* wk, int Nk,
+                          const void* wv, int Nv, void* y, int64_t ldy, const float* ss, int n_ss, int dim, float eps,
+                          void* workspace, size_t workspace_bytes, int32_t* status, b2_stream_t stream) {
+  int rc = b2::check_common(x, M, K, Nq + Nk + Nv, B2_BF16, B2_BF16, "b2_linear_qkv_rownorm");
+  if (rc) return rc;
+  B2_CHECK_ARG(Nq > 0 && Nk > 0 && Nv > 0 && n_ss > 0 && dim > 0, "b2_linear_qkv_rownorm: bad sizes");
+  B2_CHECK_ARG(ldx >= K && ldy >= (int64_t)Nq + Nk + Nv, "b2_linear_qkv_rownorm: row strides too small");
+  if (M == 0) return B2_OK;
+  B2_CHECK_ARG(wq && wk && wv && y && ss, "b2_linear_qkv_rownorm: null pointer");
+  b2::GemmSeg segs[3] = {{wq, Nq, 0}, {wk, Nk, Nq}, {wv, Nv, Nq + Nk}};
+  b2::RowNorm rn{};
+  rn.row_ss = ss;
+  rn.n_ss = n_ss;
+  rn.ss_scale = 1.f / (float)dim;
+  rn.ss_eps = eps;
+  return b2::gemm_tc(x, ldx, M, K, segs, 3, b2::kEpiStore, nullptr, y, ldy, B2_BF16, workspace, workspace_bytes,
+                     status, stream, nullptr, &rn);
+}
+
+int b2_linear_swiglu_rownorm(const void* x, int64_t ldx, int M, int K, const void* w_gate, const void* w_up, int N,
+                             void* y, int64_t ldy, const float* ss, int n_ss, int dim, float eps, void* workspace,
+                             size_t workspace_bytes, int32_t* status, b2_stream_t stream) {
+  int rc = b2::check_common(x, M, K, N, B2_BF16, B2_BF16, "b2_linear_swiglu_rownorm");
+  if (rc) return rc;
+  B2_CHECK_ARG(n_ss > 0 && dim > 0, "b2_linear_swiglu_rownorm: bad sizes");
+  B2_CHECK_ARG(ldx >= K && ldy >= N, "b2_linear_swiglu_rownorm: row strides too small");
+  if (M == 0) return B2_OK;
+  B2_CHECK_ARG(w_gate && w_up && y && ss, "b2_linear_swiglu_rownorm: null pointer");
+  b2::GemmSeg segs[2] = {{w_gate, N, 0}, {w_up, N, 0}};
+  b2::RowNorm rn{};
+  rn.row_ss = ss;
+  rn.n_ss = n_ss;
+  rn.ss_scale = 1.f / (float)dim;
+  rn.ss_eps = eps;
+  return b2::gemm_tc(x, ldx, M, K, segs, 2, b2::kEpiSwiglu, nullptr, y, ldy, B2_BF16, workspace, workspace_bytes,
+                     status, stream, nullptr, &rn);
+}
+
 }  // extern "C"

@@ -45,12 +45,27 @@ __device__ __forceinline__ void* out_base(void* y, int y_dtype, int64_t ldy, con
   return y;
 }
 
+// Deferred RMSNorm options of the tcgen05 GEMM (world size 1; see b2_linear_residual_norm).
+struct RowNorm {
+  const float* row_ss;  // consumer: per-row tile sums of h^2 [M, n_ss]
+  int n_ss;
+  float ss_scale, ss_eps;  // 1 / hidden size, epsilon
+  float* res_h;            // producer: float32 residual [M, ldh] (updated in place)
+  int64_t ldh;
+  const float* norm_w;     // producer: RMSNorm weight [N]
+  void* z;                 // producer: bf16 h * norm_w [M, ldz]
+  int64_t ldz;
+  float* ss_out;           // producer: tile sums of h^2 [M, N / 128]
+};
+
 // bf16 tcgen05 GEMM. For kEpiStore: nseg segments (1..3) concatenated along N.
 // For kEpiSwiglu: segs[0] = gate, segs[1] = up, both with n = N.
 size_t gemm_tc_workspace_bytes(int M, int n_total, int K, int epi);
+// rn: deferred RMSNorm (consumer and/or producer); the producer needs the split-K cluster
+// plan, a single segment, N % 128 == 0 and no SwiGLU, else B2_ENOTSUP before any launch.
 int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int nseg, int epi,
             const float* bias, void* y, int64_t ldy, int y_dtype, void* ws, size_t ws_bytes,
-            int32_t* status, cudaStream_t s, const Scatter* sc = nullptr);
+            int32_t* status, cudaStream_t s, const Scatter* sc = nullptr, const RowNorm* rn = nullptr);
 // Returns true when the tensor-core kernel supports the shape (K % 8 == 0, 16-byte aligned rows).
 bool gemm_tc_supported(const void* x, int64_t ldx, int K, const GemmSeg* segs, int nseg);
 

@@ -59,7 +59,39 @@ struct Params {
   const unsigned int* sc_epoch;
   int sc_R, sc_src, sc_world;
   int vec4;  // output columns in aligned groups of 4: store 4 elements per instruction
+  // Deferred RMSNorm at world size 1 (see b2_linear_residual_norm).  Consumer (row_ss set):
+  // output row m is scaled by rsqrt(sum_j row_ss[m * n_ss + j] * ss_scale + ss_eps) ahead of
+  // the epilogue (both SwiGLU halves).  Producer (res_h set, split-K cluster path only):
+  // h[m, n] += acc, z[m, n] = bf16(h * norm_w[n]), ss_out[m * ss_tiles + tile] = sum of h^2
+  // over the tile's 128 columns; nothing else is stored.
+  const float* row_ss;
+  int n_ss;
+  float ss_scale, ss_eps;
+  float* res_h;
+  int64_t ldh;
+  const float* norm_w;
+  __nv_bfloat16* z;
+  int64_t ldz;
+  float* ss_out;
+  int ss_tiles;
 };
+
+// rsqrt(mean square + eps) of row m from its per-tile partial sums, summed in tile order
+// (every caller computes the identical value); eight loads in flight per round.
+__device__ __forceinline__ float row_inv(const Params& p, int64_t m) {
+  const float* q = p.row_ss + m * p.n_ss;
+  float s = 0.f;
+  int j = 0;
+  for (; j + 8 <= p.n_ss; j += 8) {
+    float a[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) a[u] = q[j + u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) s += a[u];
+  }
+  for (; j < p.n_ss; ++j) s += q[j];
+  return rsqrtf(s * p.ss_scale + p.ss_eps);
+}
 
 __device__ __forceinline__ void store_out(const Params& p, int64_t m, int64_t col, float v) {
   int64_t idx;
@@ -285,6 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ int s_last;
+  __shared__ float s_inv[BN];  // deferred RMSNorm: per-token scale of the current unit
 
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -441,12 +474,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.splits == 1) {
         const int64_t col = (int64_t)seg_col + n;
         const float bv = (nok && p.bias) ? p.bias[col] : 0.f;
+        if (p.row_ss) {
+          for (int c = threadIdx.x - 64; c < ncols; c += 128) s_inv[c] = row_inv(p, m0 + c);
+          epilogue_sync();
+        }
         for (int c0 = 0; c0 < ncols; c0 += 16) {
           float v[16];
           tmem_ld16(acc + c0, v);
+          if (p.row_ss) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] *= s_inv[min(c0 + e, ncols - 1)];
+          }
           if (SWIGLU) {
             float uv[16];
             tmem_ld16(acc + BN + c0, uv);
+            if (p.row_ss) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) uv[e] *= s_inv[min(c0 + e, ncols - 1)];
+            }
 #pragma unroll
             for (int e = 0; e < 16; ++e) v[e] = silu_f32(v[e]) * uv[e];
           }
@@ -459,6 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        if (p.row_ss) epilogue_sync();  // s_inv is rewritten by the next unit
       } else {
         // Split-K: publish this split's float32 tile ([column][128 rows], gate then up for
         // SwiGLU), release TMEM, and let the last split of the tile reduce.
@@ -489,6 +535,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         epilogue_sync();
         if (s_last) {
           __threadfence();
+          if (p.row_ss) {
+            for (int c = threadIdx.x - 64; c < ncols; c += 128) s_inv[c] = row_inv(p, m0 + c);
+            epilogue_sync();
+          }
           const int64_t split_stride = (int64_t)p.n_tiles * p.m_tiles * tile_elems;
           const float* base = p.ws + slot * tile_elems;
           // Each epilogue warp reduces whole token columns: 32 lanes x float4 = 128 rows.
@@ -508,8 +558,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 u4.x += b.x; u4.y += b.y; u4.z += b.z; u4.w += b.w;
               }
             }
-            const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
-            const float uv[4] = {u4.x, u4.y, u4.z, u4.w};
+            const float inv = p.row_ss ? s_inv[c] : 1.f;
+            const float gv[4] = {g4.x * inv, g4.y * inv, g4.z * inv, g4.w * inv};
+            const float uv[4] = {u4.x * inv, u4.y * inv, u4.z * inv, u4.w * inv};
             float val[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) val[e] = SWIGLU ? silu_f32(gv[e]) * uv[e] : gv[e] + bv[e];
@@ -695,16 +746,27 @@ __global__ void __launch_bounds__(kThreadsCl, 1)
   const float* part0 = p.ws + (cta_lin - split) * PART_ELEMS;  // split 0 of this tile
   const int per = (ncols + p.splits - 1) / p.splits;
   const int c_lo = split * per, c_hi = min(ncols, c_lo + per);
+  __shared__ float s_inv[BN];  // deferred RMSNorm consumer: scale of each token of this slice
+  if (p.row_ss) {
+    for (int t = threadIdx.x; t < c_hi - c_lo; t += kThreadsCl) s_inv[t] = row_inv(p, m0 + c_lo + t);
+    __syncthreads();
+  }
   constexpr int VPC = BM / 4;  // float4 vectors per token column
   constexpr int U = SWIGLU ? 1 : 2;  // vectors per thread whose loads are all issued first
   const int nvec = (c_hi > c_lo ? c_hi - c_lo : 0) * VPC;
   for (int i0 = threadIdx.x; i0 < nvec; i0 += U * kThreadsCl) {
     float4 ga[U][kMaxClusterSplits], ua[U][SWIGLU ? kMaxClusterSplits : 1];
+    float4 hres[U], wres[U];  // deferred RMSNorm producer: residual and norm weight, loaded up front
 #pragma unroll
     for (int h = 0; h < U; ++h) {
       const int i = i0 + h * kThreadsCl;
       if (i >= nvec) continue;
       const float* src = part0 + (int64_t)(c_lo + i / VPC) * BM + (i % VPC) * 4;
+      if (!SWIGLU && p.res_h) {
+        const int64_t ncol = (int64_t)seg_col + local_tile * BM + (i % VPC) * 4;
+        hres[h] = *reinterpret_cast<const float4*>(p.res_h + (int64_t)(m0 + c_lo + i / VPC) * p.ldh + ncol);
+        wres[h] = *reinterpret_cast<const float4*>(p.norm_w + ncol);
+      }
 #pragma unroll
       for (int q = 0; q < kMaxClusterSplits; ++q) {
         if (q < p.splits) {
@@ -730,13 +792,32 @@ __global__ void __launch_bounds__(kThreadsCl, 1)
         }
       }
       const int nb = local_tile * BM + r4;
-      const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
-      const float uv[4] = {u4.x, u4.y, u4.z, u4.w};
+      const float inv = p.row_ss ? s_inv[c - c_lo] : 1.f;
+      const float gv[4] = {g4.x * inv, g4.y * inv, g4.z * inv, g4.w * inv};
+      const float uv[4] = {u4.x * inv, u4.y * inv, u4.z * inv, u4.w * inv};
       float val[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float bv = (!SWIGLU && p.bias && nb + e < seg_n) ? p.bias[seg_col + nb + e] : 0.f;
         val[e] = SWIGLU ? silu_f32(gv[e]) * uv[e] : gv[e] + bv;
+      }
+      if (!SWIGLU && p.res_h) {
+        // Deferred RMSNorm producer: residual add, h * w in bf16, and the tile's sum of h^2
+        // for this token (the warp's 32 lanes hold the tile's 128 columns).
+        const int64_t ncol = (int64_t)seg_col + nb;
+        float4 hv = hres[h];
+        hv.x += val[0]; hv.y += val[1]; hv.z += val[2]; hv.w += val[3];
+        *reinterpret_cast<float4*>(p.res_h + (int64_t)(m0 + c) * p.ldh + ncol) = hv;
+        const float4 wv = wres[h];
+        __nv_bfloat162 lo = __floats2bfloat162_rn(hv.x * wv.x, hv.y * wv.y);
+        __nv_bfloat162 hi = __floats2bfloat162_rn(hv.z * wv.z, hv.w * wv.w);
+        uint2 zo;
+        zo.x = *reinterpret_cast<uint32_t*>(&lo);
+        zo.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(p.z + (int64_t)(m0 + c) * p.ldz + ncol) = zo;
+        const float sq = warp_sum(hv.x * hv.x + hv.y * hv.y + hv.z * hv.z + hv.w * hv.w);
+        if (lane == 0) p.ss_out[(int64_t)(m0 + c) * p.ss_tiles + (seg_col + local_tile * BM) / BM] = sq;
+        continue;
       }
       if (p.vec4 && nb + 3 < seg_n) {
         store_out4(p, m0 + c, seg_col + nb, val);
@@ -1007,7 +1088,7 @@ bool gemm_tc_supported(const void* x, int64_t ldx, int K, const GemmSeg* segs, i
 
 int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int nseg, int epi,
             const float* bias, void* y, int64_t ldy, int y_dtype, void* ws, size_t ws_bytes,
-            int32_t* status, cudaStream_t s, const Scatter* sc) {
+            int32_t* status, cudaStream_t s, const Scatter* sc, const RowNorm* rn) {
   B2_CHECK_ARG(nseg >= 1 && nseg <= tc::kMaxSegs, "gemm_tc: bad segment count");
   B2_CHECK_ARG(gemm_tc_supported(x, ldx, K, segs, nseg),
                "gemm_tc: needs K %% 8 == 0, 16-byte aligned rows (K=%d ldx=%lld)", K, (long long)ldx);
@@ -1048,6 +1129,28 @@ int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int n
     bool v4 = ldy % 4 == 0 && (sc && sc->world > 0 ? true : ((uintptr_t)y % (4 * esz)) == 0);
     for (int i = 0; i < nseg; ++i) v4 = v4 && segs[i].col_off % 4 == 0 && segs[i].n % 4 == 0;
     p.vec4 = v4 ? 1 : 0;
+  }
+  if (rn && rn->row_ss) {
+    B2_CHECK_ARG(rn->n_ss > 0, "gemm_tc: row norm needs n_ss > 0");
+    p.row_ss = rn->row_ss;
+    p.n_ss = rn->n_ss;
+    p.ss_scale = rn->ss_scale;
+    p.ss_eps = rn->ss_eps;
+  }
+  if (rn && rn->res_h) {
+    if (!pl.cluster || sw || nseg != 1 || segs[0].n % tc::BM != 0 || !p.vec4 || y_dtype != B2_BF16)
+      return fail(B2_ENOTSUP, "gemm_tc: residual-norm epilogue needs the split-K cluster plan (M <= 128)");
+    B2_CHECK_ARG(rn->norm_w && rn->z && rn->ss_out && rn->ldh % 4 == 0 && rn->ldz % 4 == 0 &&
+                     ((uintptr_t)rn->res_h % 16) == 0 && ((uintptr_t)rn->norm_w % 16) == 0 &&
+                     ((uintptr_t)rn->z % 8) == 0,
+                 "gemm_tc: residual-norm buffers must be aligned (h, norm_w 16 B; z 8 B; strides % 4)");
+    p.res_h = rn->res_h;
+    p.ldh = rn->ldh;
+    p.norm_w = rn->norm_w;
+    p.z = static_cast<__nv_bfloat16*>(rn->z);
+    p.ldz = rn->ldz;
+    p.ss_out = rn->ss_out;
+    p.ss_tiles = segs[0].n / tc::BM;
   }
   if (sc && sc->world > 0) {
     p.sc_table = sc->table;

@@ -154,6 +154,62 @@ def linear_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
     return out
 
 
+def linear_residual_norm(x: torch.Tensor, w_packed: torch.Tensor, h: torch.Tensor, norm_w: torch.Tensor,
+                         z: torch.Tensor, ss: torch.Tensor) -> bool:
+    """Deferred-RMSNorm producer at world size 1: ``h += x @ w^T``; ``z = bf16(h * norm_w)``;
+    ``ss[m, t]`` = sum of h[m]^2 over 128-column tile t.
+
+    RowParallelLinear partial GEMM + residual add + the sums the next RMSNorm needs
+    (layers.py:147-162, 179-184; llama.py:70-75).  Returns False, having launched
+    nothing, when the shape gets no split-K cluster plan (more than 128 rows).
+    """
+    require_cuda(x, "x")
+    K = x.shape[-1]
+    x2 = x if (x.dim() == 2 and x.stride(1) == 1) else _c(x, "x").reshape(-1, K)
+    M, N = x2.shape[0], w_packed.shape[0]
+    if x2.dtype != torch.bfloat16 or w_packed.dtype != torch.bfloat16:
+        return False
+    ws, nbytes = _linear_ws(x.device, M, N, K, _lib.B2_BF16)
+    rc = _lib.lib().b2_linear_residual_norm(ptr(x2), x2.stride(0), M, K, ptr(w_packed), N, ptr(h), h.stride(0),
+                                            ptr(norm_w), ptr(z), z.stride(0), ptr(ss), ptr(ws), nbytes,
+                                            status_ptr(x.device), stream_ptr(x.device))
+    if rc == _lib.B2_ENOTSUP:
+        return False
+    check(rc, "b2_linear_residual_norm")
+    return True
+
+
+def linear_qkv_rownorm(z: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, ss: torch.Tensor,
+                       eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``linear_qkv`` of the RMS-normalised rows: z = bf16(h * w) and ss from
+    ``linear_residual_norm``; each output row is scaled by rsqrt(sum(ss) / hidden + eps)."""
+    M, K = z.shape
+    Nq, Nk, Nv = wq.shape[0], wk.shape[0], wv.shape[0]
+    if out is None:
+        out = torch.empty(M, Nq + Nk + Nv, dtype=wq.dtype, device=z.device)
+    ws, nbytes = _linear_ws(z.device, M, Nq + Nk + Nv, K, _lib.B2_BF16)
+    check(_lib.lib().b2_linear_qkv_rownorm(ptr(z), z.stride(0), M, K, ptr(wq), Nq, ptr(wk), Nk, ptr(wv), Nv,
+                                           ptr(out), out.stride(0), ptr(ss), ss.shape[1], K, float(eps), ptr(ws),
+                                           nbytes, status_ptr(z.device), stream_ptr(z.device)),
+          "b2_linear_qkv_rownorm")
+    return out
+
+
+def linear_swiglu_rownorm(z: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, ss: torch.Tensor, eps: float,
+                          out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``linear_swiglu`` of the RMS-normalised rows (see ``linear_qkv_rownorm``)."""
+    M, K = z.shape
+    N = w_gate.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=w_gate.dtype, device=z.device)
+    ws, nbytes = _linear_ws(z.device, M, N, K, _lib.B2_BF16)
+    check(_lib.lib().b2_linear_swiglu_rownorm(ptr(z), z.stride(0), M, K, ptr(w_gate), ptr(w_up), N, ptr(out),
+                                              out.stride(0), ptr(ss), ss.shape[1], K, float(eps), ptr(ws), nbytes,
+                                              status_ptr(z.device), stream_ptr(z.device)),
+          "b2_linear_swiglu_rownorm")
+    return out
+
+
 def rope_kv_write(qkv: torch.Tensor, nq: int, nkv: int, head_dim: int, rope_pos: torch.Tensor,
                   store_pos: Optional[torch.Tensor], table_index: Optional[torch.Tensor],
                   block_tables: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, q_out: torch.Tensor,

@@ -113,14 +113,23 @@ class DistributedAttention(nn.Module):
 
     # -- fused pieces shared with the model's decode/prefill path -----------------------
     def attend(self, x2d: torch.Tensor, md: TokenMetadata, pool: PhysicalKVCachePool,
-               out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """q/k/v GEMM, RoPE + KV write and paged attention; returns [T, local_heads*head_dim]."""
+               out: Optional[torch.Tensor] = None, row_ss: Optional[torch.Tensor] = None,
+               eps: float = 1e-5) -> torch.Tensor:
+        """q/k/v GEMM, RoPE + KV write and paged attention; returns [T, local_heads*head_dim].
+
+        With ``row_ss`` the input is the un-normalised ``z = h * w`` of a deferred RMSNorm
+        (``kernels.linear_residual_norm``) and the q/k/v GEMM applies the row scale.
+        """
         nq, nkv, hd = self.local_heads, self.local_kv_heads, self.head_dim
         wdt = self.q_proj.weight.dtype
         if x2d.dtype != wdt:
             x2d = x2d.to(wdt)
-        qkv = kernels.linear_qkv(x2d, self.q_proj.packed_weight(), self.k_proj.packed_weight(),
-                                 self.v_proj.packed_weight())
+        if row_ss is not None:
+            qkv = kernels.linear_qkv_rownorm(x2d, self.q_proj.packed_weight(), self.k_proj.packed_weight(),
+                                             self.v_proj.packed_weight(), row_ss, eps)
+        else:
+            qkv = kernels.linear_qkv(x2d, self.q_proj.packed_weight(), self.k_proj.packed_weight(),
+                                     self.v_proj.packed_weight())
         q = torch.empty(md.n_tokens, nq * hd, dtype=wdt, device=x2d.device)
         kernels.rope_kv_write(qkv, nq, nkv, hd, md.rope_pos, md.store_pos, md.table_index, md.tables,
                               self.rope.cos_cached, self.rope.sin_cached, q, pool.k_cache, pool.v_cache,

@@ -168,13 +168,27 @@ class DistributedLLaMAModel(nn.Module):
         h = kernels.embedding(ids, self.embed_tokens.weight, out_dtype=torch.float32)
         xn = torch.empty(T, H, dtype=wdt, device=self.device)
         kernels.rmsnorm(h, self.layers[0].input_layernorm.weight, eps, out=xn)
+        # Deferred RMSNorm (bf16, <= 128 rows): the row-parallel GEMM adds the residual and
+        # leaves z = h * w plus per-tile sums of h^2; the next GEMM applies the row scale.
+        # ready: the next GEMM's input is (z, ss) rather than the normalised xn.
+        fused = wdt == torch.bfloat16 and T <= 128 and H % 128 == 0
+        z = torch.empty(T, H, dtype=wdt, device=self.device) if fused else None
+        ss = torch.empty(T, H // 128, dtype=torch.float32, device=self.device) if fused else None
+        ready = False
         n = len(self.layers)
         for i, layer in enumerate(self.layers):
-            attn = layer.self_attn.attend(xn, md, kv_pool)
-            _row_parallel_norm(layer.self_attn.out_proj, attn, h, layer.post_attention_layernorm.weight, eps, xn)
-            inter = layer.mlp.gate_up(xn)
+            attn = layer.self_attn.attend(z if ready else xn, md, kv_pool, row_ss=ss if ready else None, eps=eps)
+            post_w = layer.post_attention_layernorm.weight
+            ready = fused and kernels.linear_residual_norm(attn, layer.self_attn.out_proj.packed_weight(), h, post_w,
+                                                           z, ss)
+            if not ready:
+                _row_parallel_norm(layer.self_attn.out_proj, attn, h, post_w, eps, xn)
+            inter = layer.mlp.gate_up(z if ready else xn, row_ss=ss if ready else None, eps=eps)
             next_w = self.layers[i + 1].input_layernorm.weight if i + 1 < n else self.norm.weight
-            _row_parallel_norm(layer.mlp.down_proj, inter, h, next_w, eps, xn)
+            ready = fused and i + 1 < n and kernels.linear_residual_norm(inter, layer.mlp.down_proj.packed_weight(),
+                                                                         h, next_w, z, ss)
+            if not ready:
+                _row_parallel_norm(layer.mlp.down_proj, inter, h, next_w, eps, xn)
             if trace is not None:
                 trace.append(h.clone())
         return xn

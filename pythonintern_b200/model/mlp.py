@@ -42,8 +42,13 @@ class DistributedMLP(nn.Module):
         self.communicator = communicator
         self.down_proj.set_communicator(communicator)
 
-    def gate_up(self, x2d: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """``silu(x Wg) * (x Wu)`` for [T, hidden] rows (mlp.py:80-82)."""
+    def gate_up(self, x2d: torch.Tensor, out: Optional[torch.Tensor] = None, row_ss: Optional[torch.Tensor] = None,
+                eps: float = 1e-5) -> torch.Tensor:
+        """``silu(x Wg) * (x Wu)`` for [T, hidden] rows (mlp.py:80-82); with ``row_ss`` the rows
+        are a deferred RMSNorm's ``z = h * w`` and the row scale is applied in the GEMM."""
+        if row_ss is not None:
+            return kernels.linear_swiglu_rownorm(x2d, self.gate_proj.packed_weight(), self.up_proj.packed_weight(),
+                                                 row_ss, eps, out=out)
         return kernels.linear_swiglu(x2d, self.gate_proj.packed_weight(), self.up_proj.packed_weight(), out=out)
 
     def forward(self, x: torch.Tensor, step_id: int = 0) -> torch.Tensor:

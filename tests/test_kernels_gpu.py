@@ -179,6 +179,43 @@ def test_large_gemm_repeated_calls_are_identical():
     assert rel(to_np(y2), to_np(x) @ to_np(wg).T) < 8e-3
 
 
+@pytest.mark.parametrize("M", [128, 5])
+def test_deferred_rmsnorm_producer_and_consumers(M):
+    """Row-parallel GEMM + residual add leaving z = h * w and per-tile sums of h^2, then
+    q|k|v and SwiGLU GEMMs that apply the RMS scale per row: against float64 on the same
+    bf16 inputs (the normalised GEMM input is never rounded, so compare the scaled GEMM
+    of z, and the explicit rmsnorm + GEMM path at the bf16 tolerance)."""
+    H, K, I, eps = 4096, 4096, 1024, 1e-5
+    x = torch.randn(M, K, generator=g(M + 1)).to(DEV, torch.bfloat16)
+    w = (torch.randn(H, K, generator=g(M + 2)) / math.sqrt(K)).to(DEV, torch.bfloat16)
+    h0 = torch.randn(M, H, generator=g(M + 3)).to(DEV)
+    nw = (1.0 + 0.1 * torch.randn(H, generator=g(M + 4))).to(DEV)
+    h = h0.clone()
+    z = torch.empty(M, H, dtype=torch.bfloat16, device=DEV)
+    ss = torch.empty(M, H // 128, device=DEV)
+    assert kernels.linear_residual_norm(x, w, h, nw, z, ss)
+    torch.cuda.synchronize()
+    _lib.check_device_status(DEV, "residual norm")
+    h_ref = to_np(h0) + to_np(x) @ to_np(w).T
+    assert rel(to_np(h), h_ref) < 3e-5
+    assert rel(to_np(z), h_ref * to_np(nw)) < 8e-3
+    assert rel(to_np(ss), (h_ref.reshape(M, H // 128, 128) ** 2).sum(-1)) < 1e-4
+    inv = 1.0 / np.sqrt((to_np(ss).sum(-1) / H) + eps)
+    wg = (torch.randn(I, H, generator=g(M + 5)) / math.sqrt(H)).to(DEV, torch.bfloat16)
+    wu = (torch.randn(I, H, generator=g(M + 6)) / math.sqrt(H)).to(DEV, torch.bfloat16)
+    y = kernels.linear_swiglu_rownorm(z, wg, wu, ss, eps)
+    zn = to_np(z)
+    want = oracle.silu(inv[:, None] * (zn @ to_np(wg).T)) * (inv[:, None] * (zn @ to_np(wu).T))
+    assert rel(to_np(y), want) < 8e-3
+    xn = kernels.rmsnorm(h, nw, eps, out_dtype=torch.bfloat16)  # the unfused path
+    assert rel(to_np(y), to_np(kernels.linear_swiglu(xn, wg, wu))) < 2e-2
+    wq, wk, wv = [(torch.randn(n, H, generator=g(M + 7 + i)) / math.sqrt(H)).to(DEV, torch.bfloat16)
+                  for i, n in enumerate((512, 128, 128))]
+    q = kernels.linear_qkv_rownorm(z, wq, wk, wv, ss, eps)
+    want = inv[:, None] * (zn @ np.concatenate([to_np(wq), to_np(wk), to_np(wv)]).T)
+    assert rel(to_np(q), want) < 8e-3
+
+
 def test_split_k_workspace_shared_across_shapes():
     """Launches with different tile counts share one workspace; none may read another's partials."""
     shapes = [(3, 5632, 2048, "swiglu"), (37, 2560, 2048, "linear"), (64, 256, 8192, "linear"),
