@@ -120,6 +120,20 @@ int b2_linear_swiglu_rownorm(const void* x, int64_t ldx, int M, int K, const voi
                              void* y, int64_t ldy, const float* ss, int n_ss, int dim, float eps, void* workspace,
                              size_t workspace_bytes, int32_t* status, b2_stream_t stream);
 
+/* q|k|v GEMM with RoPE and the paged KV write in its epilogue: b2_linear_qkv (or, with ss
+ * set, b2_linear_qkv_rownorm) followed by b2_rope_kv_write, without the intermediate
+ * [M, (nq + 2 nkv) * 128] buffer (attention.py:156-158 then :46-63, :166-184).  The
+ * outputs are bit-identical to the two calls.  head_dim must be 128 and M <= 128; returns
+ * B2_ENOTSUP, before launching anything, otherwise or when the shape gets no split-K
+ * cluster plan (the caller then makes the two calls).  bf16 only. */
+int b2_linear_qkv_rope_kv(const void* x, int64_t ldx, int M, int K, const void* wq, const void* wk, const void* wv,
+                          int nq, int nkv, int head_dim, const float* ss, int n_ss, int dim, float eps,
+                          const int64_t* rope_pos, const int64_t* store_pos, const int32_t* table_index,
+                          const int32_t* block_tables, int table_stride, int num_blocks, int block_size,
+                          const float* cos, const float* sin, int max_seq_len, void* q_out, void* k_cache,
+                          void* v_cache, int layer, void* workspace, size_t workspace_bytes, int32_t* status,
+                          b2_stream_t stream);
+
 /* ---------------------------------------------------------------- RoPE + paged KV write
  * For token i (0 <= i < n_tokens) with row = table_index ? table_index[i] : i:
  *   q_out[i, h, :]   = rope(qkv[i, q-head h], rope_pos[i])                 (attention.py:46-63,161)

@@ -81,6 +81,11 @@ _SIGS = {
     "b2_linear_swiglu_rownorm": (_c_int, [_c_void_p, _c_i64, _c_int, _c_int, _c_void_p, _c_void_p, _c_int,
                                           _c_void_p, _c_i64, _c_void_p, _c_int, _c_int, _c_float, _c_void_p,
                                           _c_size, _c_void_p, _c_void_p]),
+    "b2_linear_qkv_rope_kv": (_c_int, [_c_void_p, _c_i64, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p,
+                                       _c_int, _c_int, _c_int, _c_void_p, _c_int, _c_int, _c_float,
+                                       _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_int,
+                                       _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int,
+                                       _c_void_p, _c_size, _c_void_p, _c_void_p]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -125,7 +130,8 @@ launch_count = 0
 _LAUNCHING = {"b2_embedding", "b2_rmsnorm", "b2_linear", "b2_linear_qkv", "b2_linear_swiglu",
               "b2_rope_kv_write", "b2_paged_attention", "b2_argmax", "b2_allreduce_sum", "b2_allreduce_rmsnorm",
               "b2_row_parallel_linear", "b2_allreduce_rmsnorm_sharded", "b2_paged_attention_noalloc",
-              "b2_argmax_allgather", "b2_linear_residual_norm", "b2_linear_qkv_rownorm", "b2_linear_swiglu_rownorm"}
+              "b2_argmax_allgather", "b2_linear_residual_norm", "b2_linear_qkv_rownorm", "b2_linear_swiglu_rownorm",
+              "b2_linear_qkv_rope_kv"}
 
 
 def check(rc: int, what: str = ""):

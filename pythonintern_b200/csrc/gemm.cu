@@ -133,4 +133,52 @@ int b2_linear_swiglu_rownorm(const void* x, int64_t ldx, int M, int K, const voi
                      status, stream, nullptr, &rn);
 }
 
+int b2_linear_qkv_rope_kv(const void* x, int64_t ldx, int M, int K, const void* wq, const void* wk, const void* wv,
+                          int nq, int nkv, int head_dim, const float* ss, int n_ss, int dim, float eps,
+                          const int64_t* rope_pos, const int64_t* store_pos, const int32_t* table_index,
+                          const int32_t* block_tables, int table_stride, int num_blocks, int block_size,
+                          const float* cos, const float* sin, int max_seq_len, void* q_out, void* k_cache,
+                          void* v_cache, int layer, void* workspace, size_t workspace_bytes, int32_t* status,
+                          b2_stream_t stream) {
+  int rc = b2::check_common(x, M, K, (nq + 2 * nkv) * head_dim, B2_BF16, B2_BF16, "b2_linear_qkv_rope_kv");
+  if (rc) return rc;
+  B2_CHECK_ARG(nq > 0 && nkv > 0 && ldx >= K, "b2_linear_qkv_rope_kv: bad sizes");
+  B2_CHECK_ARG(num_blocks > 0 && block_size > 0 && table_stride > 0 && layer >= 0 && max_seq_len > 0,
+               "b2_linear_qkv_rope_kv: bad cache geometry");
+  if (M == 0) return B2_OK;
+  if (head_dim != 128 || M > 128)
+    return b2::fail(B2_ENOTSUP, "b2_linear_qkv_rope_kv: needs head_dim 128 and at most 128 rows");
+  B2_CHECK_ARG(wq && wk && wv && rope_pos && block_tables && cos && sin && q_out && k_cache && v_cache,
+               "b2_linear_qkv_rope_kv: null pointer");
+  B2_CHECK_ARG(!ss || (n_ss > 0 && dim > 0), "b2_linear_qkv_rope_kv: bad row-norm sizes");
+  b2::GemmSeg segs[3] = {{wq, nq * head_dim, 0}, {wk, nkv * head_dim, nq * head_dim},
+                         {wv, nkv * head_dim, (nq + nkv) * head_dim}};
+  b2::RowNorm rn{};
+  if (ss) {
+    rn.row_ss = ss;
+    rn.n_ss = n_ss;
+    rn.ss_scale = 1.f / (float)dim;
+    rn.ss_eps = eps;
+  }
+  b2::RopeKV rk{};
+  rk.nq = nq;
+  rk.nkv = nkv;
+  rk.rope_pos = rope_pos;
+  rk.store_pos = store_pos;
+  rk.table_index = table_index;
+  rk.tables = block_tables;
+  rk.table_stride = table_stride;
+  rk.num_blocks = num_blocks;
+  rk.block_size = block_size;
+  rk.max_seq_len = max_seq_len;
+  rk.cos_t = cos;
+  rk.sin_t = sin;
+  rk.q_out = q_out;
+  rk.k_cache = k_cache;
+  rk.v_cache = v_cache;
+  rk.layer_off = (int64_t)num_blocks * block_size * nkv * head_dim * layer;
+  return b2::gemm_tc(x, ldx, M, K, segs, 3, b2::kEpiStore, nullptr, nullptr, (nq + 2 * nkv) * head_dim, B2_BF16,
+                     workspace, workspace_bytes, status, stream, nullptr, ss ? &rn : nullptr, &rk);
+}
+
 }  // extern "C"

@@ -58,6 +58,23 @@ struct RowNorm {
   float* ss_out;           // producer: tile sums of h^2 [M, N / 128]
 };
 
+// Fused RoPE + paged KV write epilogue of the q|k|v GEMM (head_dim 128: one 128-row weight
+// tile per head; see b2_linear_qkv_rope_kv).  Mirrors rope_kv_write_kernel argument for argument.
+struct RopeKV {
+  int nq, nkv;
+  const int64_t* rope_pos;
+  const int64_t* store_pos;
+  const int32_t* table_index;
+  const int32_t* tables;
+  int table_stride, num_blocks, block_size, max_seq_len;
+  const float* cos_t;
+  const float* sin_t;
+  void* q_out;
+  void* k_cache;
+  void* v_cache;
+  int64_t layer_off;  // elements from the pool start to this layer
+};
+
 // bf16 tcgen05 GEMM. For kEpiStore: nseg segments (1..3) concatenated along N.
 // For kEpiSwiglu: segs[0] = gate, segs[1] = up, both with n = N.
 size_t gemm_tc_workspace_bytes(int M, int n_total, int K, int epi);
@@ -65,7 +82,8 @@ size_t gemm_tc_workspace_bytes(int M, int n_total, int K, int epi);
 // plan, a single segment, N % 128 == 0 and no SwiGLU, else B2_ENOTSUP before any launch.
 int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int nseg, int epi,
             const float* bias, void* y, int64_t ldy, int y_dtype, void* ws, size_t ws_bytes,
-            int32_t* status, cudaStream_t s, const Scatter* sc = nullptr, const RowNorm* rn = nullptr);
+            int32_t* status, cudaStream_t s, const Scatter* sc = nullptr, const RowNorm* rn = nullptr,
+            const RopeKV* rk = nullptr);
 // Returns true when the tensor-core kernel supports the shape (K % 8 == 0, 16-byte aligned rows).
 bool gemm_tc_supported(const void* x, int64_t ldx, int K, const GemmSeg* segs, int nseg);
 

@@ -74,6 +74,21 @@ struct Params {
   int64_t ldz;
   float* ss_out;
   int ss_tiles;
+  // Fused RoPE + paged KV write (q|k|v GEMM, head_dim 128): tile h < nq is q head h, then
+  // the k heads, then the v heads; nothing else is stored.
+  int rope;
+  int nq, nkv;
+  const int64_t* rope_pos;
+  const int64_t* store_pos;
+  const int32_t* table_index;
+  const int32_t* tables;
+  int table_stride, num_blocks, block_size, max_seq_len;
+  const float* cos_t;
+  const float* sin_t;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int64_t layer_off;
 };
 
 // rsqrt(mean square + eps) of row m from its per-tile partial sums, summed in tile order
@@ -747,8 +762,26 @@ __global__ void __launch_bounds__(kThreadsCl, 1)
   const int per = (ncols + p.splits - 1) / p.splits;
   const int c_lo = split * per, c_hi = min(ncols, c_lo + per);
   __shared__ float s_inv[BN];  // deferred RMSNorm consumer: scale of each token of this slice
-  if (p.row_ss) {
-    for (int t = threadIdx.x; t < c_hi - c_lo; t += kThreadsCl) s_inv[t] = row_inv(p, m0 + c_lo + t);
+  __shared__ int s_pos[BN];    // fused RoPE: position of each token (-1: out of range)
+  __shared__ int64_t s_slot[BN];  // fused RoPE: element offset of its KV slot (-1: out of range)
+  if (p.row_ss || p.rope) {
+    for (int t = threadIdx.x; t < c_hi - c_lo; t += kThreadsCl) {
+      const int tok = m0 + c_lo + t;
+      if (p.row_ss) s_inv[t] = row_inv(p, tok);
+      if (p.rope) {
+        const int64_t pos = p.rope_pos[tok];
+        const int64_t ps = p.store_pos ? p.store_pos[tok] : pos;
+        const int row = p.table_index ? p.table_index[tok] : tok;
+        const bool pos_ok = pos >= 0 && pos < p.max_seq_len;
+        int64_t blk = -1;
+        if (ps >= 0 && (ps / p.block_size) < p.table_stride)
+          blk = p.tables[(int64_t)row * p.table_stride + ps / p.block_size];
+        const bool slot_ok = blk >= 0 && blk < p.num_blocks;
+        if (tile == 0 && !(pos_ok && slot_ok)) raise_status(p.status, B2_DEV_RANGE);
+        s_pos[t] = pos_ok ? (int)pos : -1;
+        s_slot[t] = slot_ok ? p.layer_off + ((blk * p.block_size + ps % p.block_size) * p.nkv) * (int64_t)BM : -1;
+      }
+    }
     __syncthreads();
   }
   constexpr int VPC = BM / 4;  // float4 vectors per token column
@@ -757,11 +790,19 @@ __global__ void __launch_bounds__(kThreadsCl, 1)
   for (int i0 = threadIdx.x; i0 < nvec; i0 += U * kThreadsCl) {
     float4 ga[U][kMaxClusterSplits], ua[U][SWIGLU ? kMaxClusterSplits : 1];
     float4 hres[U], wres[U];  // deferred RMSNorm producer: residual and norm weight, loaded up front
+    float4 crope[U], srope[U];  // fused RoPE: cos / sin of the token's position, loaded up front
 #pragma unroll
     for (int h = 0; h < U; ++h) {
       const int i = i0 + h * kThreadsCl;
       if (i >= nvec) continue;
       const float* src = part0 + (int64_t)(c_lo + i / VPC) * BM + (i % VPC) * 4;
+      if (!SWIGLU && p.rope && tile < p.nq + p.nkv) {
+        const int pos = s_pos[i / VPC];
+        if (pos >= 0) {
+          crope[h] = *reinterpret_cast<const float4*>(p.cos_t + (int64_t)pos * BM + (i % VPC) * 4);
+          srope[h] = *reinterpret_cast<const float4*>(p.sin_t + (int64_t)pos * BM + (i % VPC) * 4);
+        }
+      }
       if (!SWIGLU && p.res_h) {
         const int64_t ncol = (int64_t)seg_col + local_tile * BM + (i % VPC) * 4;
         hres[h] = *reinterpret_cast<const float4*>(p.res_h + (int64_t)(m0 + c_lo + i / VPC) * p.ldh + ncol);
@@ -800,6 +841,47 @@ __global__ void __launch_bounds__(kThreadsCl, 1)
       for (int e = 0; e < 4; ++e) {
         const float bv = (!SWIGLU && p.bias && nb + e < seg_n) ? p.bias[seg_col + nb + e] : 0.f;
         val[e] = SWIGLU ? silu_f32(gv[e]) * uv[e] : gv[e] + bv;
+      }
+      if (!SWIGLU && p.rope) {
+        // Fused RoPE + paged KV write: the GEMM output rounded to bf16 (as the q|k|v buffer
+        // would hold it) is rotated with the same two-rounding formula as rope_kv_write_kernel;
+        // the rotate-half partner of columns d..d+3 sits in lane ^ 16 of this warp.
+        const int head = tile;
+        const int tok = m0 + c;
+        float x[4], xp[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] = __bfloat162float(__float2bfloat16_rn(val[e]));
+#pragma unroll
+        for (int e = 0; e < 4; ++e) xp[e] = __shfl_xor_sync(0xffffffffu, x[e], 16);
+        if (s_pos[c - c_lo] < 0) continue;
+        const int64_t slot_off = s_slot[c - c_lo];
+        const bool slot_ok = slot_off >= 0;
+        float o[4];
+        if (head < p.nq + p.nkv) {
+          const bool lower = r4 < BM / 2;
+          const float ct[4] = {crope[h].x, crope[h].y, crope[h].z, crope[h].w};
+          const float st[4] = {srope[h].x, srope[h].y, srope[h].z, srope[h].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e)  // lower: x1*cos - x2*sin;  upper: x2*cos + x1*sin
+            o[e] = __fadd_rn(__fmul_rn(x[e], ct[e]), __fmul_rn(lower ? -xp[e] : xp[e], st[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[e] = x[e];
+        }
+        __nv_bfloat16* dst;
+        if (head < p.nq) {
+          dst = p.q_out + ((int64_t)tok * p.nq + head) * BM + r4;
+        } else {
+          if (!slot_ok) continue;
+          dst = head < p.nq + p.nkv ? p.k_cache + slot_off + (int64_t)(head - p.nq) * BM + r4
+                                    : p.v_cache + slot_off + (int64_t)(head - p.nq - p.nkv) * BM + r4;
+        }
+        __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]), hi = __floats2bfloat162_rn(o[2], o[3]);
+        uint2 ov;
+        ov.x = *reinterpret_cast<uint32_t*>(&lo);
+        ov.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(dst) = ov;
+        continue;
       }
       if (!SWIGLU && p.res_h) {
         // Deferred RMSNorm producer: residual add, h * w in bf16, and the tile's sum of h^2
@@ -1088,7 +1170,7 @@ bool gemm_tc_supported(const void* x, int64_t ldx, int K, const GemmSeg* segs, i
 
 int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int nseg, int epi,
             const float* bias, void* y, int64_t ldy, int y_dtype, void* ws, size_t ws_bytes,
-            int32_t* status, cudaStream_t s, const Scatter* sc, const RowNorm* rn) {
+            int32_t* status, cudaStream_t s, const Scatter* sc, const RowNorm* rn, const RopeKV* rk) {
   B2_CHECK_ARG(nseg >= 1 && nseg <= tc::kMaxSegs, "gemm_tc: bad segment count");
   B2_CHECK_ARG(gemm_tc_supported(x, ldx, K, segs, nseg),
                "gemm_tc: needs K %% 8 == 0, 16-byte aligned rows (K=%d ldx=%lld)", K, (long long)ldx);
@@ -1151,6 +1233,33 @@ int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int n
     p.ldz = rn->ldz;
     p.ss_out = rn->ss_out;
     p.ss_tiles = segs[0].n / tc::BM;
+  }
+  if (rk) {
+    if (!pl.cluster || sw || nseg != 3 || y_dtype != B2_BF16)
+      return fail(B2_ENOTSUP, "gemm_tc: fused RoPE epilogue needs the split-K cluster plan (M <= 128)");
+    B2_CHECK_ARG(segs[0].n == rk->nq * tc::BM && segs[1].n == rk->nkv * tc::BM && segs[2].n == rk->nkv * tc::BM,
+                 "gemm_tc: fused RoPE needs head_dim 128 (one weight tile per head)");
+    B2_CHECK_ARG(((uintptr_t)rk->q_out % 8) == 0 && ((uintptr_t)rk->k_cache % 8) == 0 &&
+                     ((uintptr_t)rk->v_cache % 8) == 0 && ((uintptr_t)rk->cos_t % 16) == 0 &&
+                     ((uintptr_t)rk->sin_t % 16) == 0,
+                 "gemm_tc: fused RoPE buffers must be aligned (outputs 8 B, tables 16 B)");
+    p.rope = 1;
+    p.nq = rk->nq;
+    p.nkv = rk->nkv;
+    p.rope_pos = rk->rope_pos;
+    p.store_pos = rk->store_pos;
+    p.table_index = rk->table_index;
+    p.tables = rk->tables;
+    p.table_stride = rk->table_stride;
+    p.num_blocks = rk->num_blocks;
+    p.block_size = rk->block_size;
+    p.max_seq_len = rk->max_seq_len;
+    p.cos_t = rk->cos_t;
+    p.sin_t = rk->sin_t;
+    p.q_out = static_cast<__nv_bfloat16*>(rk->q_out);
+    p.k_cache = static_cast<__nv_bfloat16*>(rk->k_cache);
+    p.v_cache = static_cast<__nv_bfloat16*>(rk->v_cache);
+    p.layer_off = rk->layer_off;
   }
   if (sc && sc->world > 0) {
     p.sc_table = sc->table;

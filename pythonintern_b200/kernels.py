@@ -210,6 +210,33 @@ def linear_swiglu_rownorm(z: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Ten
     return out
 
 
+def linear_qkv_rope_kv(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, nq: int, nkv: int,
+                       head_dim: int, rope_pos: torch.Tensor, store_pos: Optional[torch.Tensor],
+                       table_index: Optional[torch.Tensor], block_tables: torch.Tensor, cos: torch.Tensor,
+                       sin: torch.Tensor, q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                       layer: int, row_ss: Optional[torch.Tensor] = None, eps: float = 1e-5) -> bool:
+    """``linear_qkv`` (or ``linear_qkv_rownorm`` with ``row_ss``) + ``rope_kv_write`` in one
+    launch, bit-identical to the two.  Returns False, having launched nothing, when the
+    shape has no fused form (head_dim != 128, more than 128 rows, or no cluster plan)."""
+    M, K = x.shape
+    if x.dtype != torch.bfloat16 or head_dim != 128 or M > 128:
+        return False
+    _, NB, bs, ckv, chd = k_cache.shape
+    assert ckv == nkv and chd == head_dim, "cache geometry does not match the heads"
+    assert block_tables.dtype == torch.int32 and block_tables.is_contiguous()
+    N = (nq + 2 * nkv) * head_dim
+    ws, nbytes = _linear_ws(x.device, M, N, K, _lib.B2_BF16)
+    rc = _lib.lib().b2_linear_qkv_rope_kv(
+        ptr(x), x.stride(0), M, K, ptr(wq), ptr(wk), ptr(wv), nq, nkv, head_dim, ptr(row_ss),
+        row_ss.shape[1] if row_ss is not None else 0, K, float(eps), ptr(rope_pos), ptr(store_pos),
+        ptr(table_index), ptr(block_tables), block_tables.shape[1], NB, bs, ptr(cos), ptr(sin), cos.shape[0],
+        ptr(q_out), ptr(k_cache), ptr(v_cache), layer, ptr(ws), nbytes, status_ptr(x.device), stream_ptr(x.device))
+    if rc == _lib.B2_ENOTSUP:
+        return False
+    check(rc, "b2_linear_qkv_rope_kv")
+    return True
+
+
 def rope_kv_write(qkv: torch.Tensor, nq: int, nkv: int, head_dim: int, rope_pos: torch.Tensor,
                   store_pos: Optional[torch.Tensor], table_index: Optional[torch.Tensor],
                   block_tables: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, q_out: torch.Tensor,

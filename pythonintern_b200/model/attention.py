@@ -124,16 +124,20 @@ class DistributedAttention(nn.Module):
         wdt = self.q_proj.weight.dtype
         if x2d.dtype != wdt:
             x2d = x2d.to(wdt)
-        if row_ss is not None:
-            qkv = kernels.linear_qkv_rownorm(x2d, self.q_proj.packed_weight(), self.k_proj.packed_weight(),
-                                             self.v_proj.packed_weight(), row_ss, eps)
-        else:
-            qkv = kernels.linear_qkv(x2d, self.q_proj.packed_weight(), self.k_proj.packed_weight(),
-                                     self.v_proj.packed_weight())
+        wq, wk, wv = self.q_proj.packed_weight(), self.k_proj.packed_weight(), self.v_proj.packed_weight()
         q = torch.empty(md.n_tokens, nq * hd, dtype=wdt, device=x2d.device)
-        kernels.rope_kv_write(qkv, nq, nkv, hd, md.rope_pos, md.store_pos, md.table_index, md.tables,
-                              self.rope.cos_cached, self.rope.sin_cached, q, pool.k_cache, pool.v_cache,
-                              self.layer_idx)
+        # q|k|v GEMM with RoPE and the KV write in its epilogue where the shape allows it
+        # (bit-identical to the GEMM + rope_kv_write pair below)
+        if not kernels.linear_qkv_rope_kv(x2d, wq, wk, wv, nq, nkv, hd, md.rope_pos, md.store_pos, md.table_index,
+                                          md.tables, self.rope.cos_cached, self.rope.sin_cached, q, pool.k_cache,
+                                          pool.v_cache, self.layer_idx, row_ss=row_ss, eps=eps):
+            if row_ss is not None:
+                qkv = kernels.linear_qkv_rownorm(x2d, wq, wk, wv, row_ss, eps)
+            else:
+                qkv = kernels.linear_qkv(x2d, wq, wk, wv)
+            kernels.rope_kv_write(qkv, nq, nkv, hd, md.rope_pos, md.store_pos, md.table_index, md.tables,
+                                  self.rope.cos_cached, self.rope.sin_cached, q, pool.k_cache, pool.v_cache,
+                                  self.layer_idx)
         splits = kernels.attention_splits(md.n_tokens, nkv, md.max_ctx, pool.block_size, x2d.device)
         return kernels.paged_attention(q, nq, nkv, hd, pool.k_cache, pool.v_cache, self.layer_idx, md.tables,
                                        md.table_index, md.ctx_lens, md.compat_pad, 1.0 / math.sqrt(hd),

@@ -216,6 +216,38 @@ def test_deferred_rmsnorm_producer_and_consumers(M):
     assert rel(to_np(q), want) < 8e-3
 
 
+@pytest.mark.parametrize("M,nq,nkv,rownorm", [(128, 32, 8, False), (128, 4, 1, True), (7, 8, 2, True)])
+def test_fused_qkv_rope_kv_is_bit_identical(M, nq, nkv, rownorm):
+    """q|k|v GEMM with RoPE and the paged KV write in its epilogue equals the GEMM followed
+    by rope_kv_write, bit for bit: q, and every K/V slot of the pool."""
+    hd, K, bs, L, eps = 128, 1024, 16, 2, 1e-5
+    x = torch.randn(M, K, generator=g(M + 11)).to(DEV, torch.bfloat16)
+    wq, wk, wv = [(torch.randn(n * hd, K, generator=g(M + 12 + i)) / math.sqrt(K)).to(DEV, torch.bfloat16)
+                  for i, n in enumerate((nq, nkv, nkv))]
+    NB = M * 4 + 3
+    tables = torch.randperm(NB - 3, generator=g(5))[: M * 4].view(M, 4).to(torch.int32).to(DEV)
+    pos = torch.randint(0, 4 * bs, (M,), generator=g(6)).to(DEV)
+    tab_cos = torch.randn(512, hd, generator=g(7)).to(DEV)
+    tab_sin = torch.randn(512, hd, generator=g(8)).to(DEV)
+    ss = torch.rand(M, K // 128, generator=g(9)).to(DEV) * 50 if rownorm else None
+    outs = []
+    for fused in (True, False):
+        kc = torch.zeros(L, NB, bs, nkv, hd, dtype=torch.bfloat16, device=DEV)
+        vc = torch.zeros_like(kc)
+        q = torch.empty(M, nq * hd, dtype=torch.bfloat16, device=DEV)
+        if fused:
+            assert kernels.linear_qkv_rope_kv(x, wq, wk, wv, nq, nkv, hd, pos, None, None, tables, tab_cos,
+                                              tab_sin, q, kc, vc, 1, row_ss=ss, eps=eps)
+        else:
+            qkv = kernels.linear_qkv_rownorm(x, wq, wk, wv, ss, eps) if rownorm else kernels.linear_qkv(x, wq, wk, wv)
+            kernels.rope_kv_write(qkv, nq, nkv, hd, pos, None, None, tables, tab_cos, tab_sin, q, kc, vc, 1)
+        torch.cuda.synchronize()
+        _lib.check_device_status(DEV, "qkv rope")
+        outs.append((q, kc, vc))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+
 def test_split_k_workspace_shared_across_shapes():
     """Launches with different tile counts share one workspace; none may read another's partials."""
     shapes = [(3, 5632, 2048, "swiglu"), (37, 2560, 2048, "linear"), (64, 256, 8192, "linear"),
