@@ -125,3 +125,42 @@ def test_package_has_no_cpu_compute_path():
     from pythonintern_b200 import kernels
     with pytest.raises(Exception):
         kernels.linear(torch.zeros(2, 8), torch.zeros(4, 8))
+
+
+def test_decode_graph_packs_only_changed_table_rows():
+    """The decode graph's host packing reuses the previous step's rows and rewrites a row
+    only when its block table changed (grown, shrunk or edited), padding with -1."""
+    from types import SimpleNamespace
+    from pythonintern_b200.worker.graphs import DecodeGraph, _layout
+    B, W = 3, 8
+    g = SimpleNamespace(batch=B, width=W, _tab=np.full((B, W), -1, dtype=np.int32), _rows=[None] * B)
+    total = _layout(B, W)[-1]
+    out = np.zeros(total, dtype=np.uint8)
+    o_tab = _layout(B, W)[3]
+
+    def tabs():
+        return out[o_tab:o_tab + 4 * B * W].view(np.int32).reshape(B, W)
+    tables = [[5, 6], [7], [1, 2, 3]]
+    DecodeGraph.pack(g, [1, 2, 3], [10, 11, 12], tables, out)
+    assert tabs().tolist() == [[5, 6] + [-1] * 6, [7] + [-1] * 7, [1, 2, 3] + [-1] * 5]
+    tables = [[5, 6, 9], [4], np.array([1, 2, 3])]  # grown, edited, unchanged (as an array)
+    DecodeGraph.pack(g, [1, 2, 3], [10, 11, 12], tables, out)
+    assert tabs().tolist() == [[5, 6, 9] + [-1] * 5, [4] + [-1] * 7, [1, 2, 3] + [-1] * 5]
+    DecodeGraph.pack(g, [1, 2, 3], [10, 11, 12], [[5], [4], [1, 2, 3]], out)  # shrunk
+    assert tabs()[0].tolist() == [5] + [-1] * 7
+    with pytest.raises(ValueError):
+        DecodeGraph.pack(g, [1, 2, 3], [10, 11, 12], [[0] * (W + 1), [4], [1]], out)
+
+
+def test_vocab_slices_cover_the_vocabulary_once():
+    """Each rank's lm_head rows for the vocab-parallel greedy step: contiguous, disjoint,
+    covering [0, V) in rank order (so rank order is vocabulary order)."""
+    from types import SimpleNamespace
+    from pythonintern_b200.model.llama import DistributedLLaMAModel
+    for V in (1024, 32000, 128256, 1001):
+        for t in (1, 2, 4, 8):
+            spans = [DistributedLLaMAModel.vocab_slice(SimpleNamespace(config=SimpleNamespace(vocab_size=V),
+                                                                       world_size=t, rank=r)) for r in range(t)]
+            assert spans[0][0] == 0 and spans[-1][1] == V
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            assert all(e > s for s, e in spans)
