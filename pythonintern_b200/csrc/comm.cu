@@ -272,7 +272,10 @@ template <typename T>
 __global__ void __launch_bounds__(512) allreduce_rmsnorm_sharded_kernel(CommView v, int rows, int R, int dim, float* h_slice,
                                                  const float* __restrict__ w, float eps, T* __restrict__ y,
                                                  int64_t timeout_ns, int32_t* status) {
-  pdl_wait();
+  // No griddepcontrol.wait: everything this kernel reads from the preceding GEMM arrives
+  // through the sentinel-checked receive slot, and the rest (epoch, extents, residual
+  // slice) was last written by the previous call of this kernel, which the GEMM itself
+  // waited for.  So its CTAs start polling as soon as the GEMM's CTAs free their SMs.
   pdl_trigger();
   __shared__ float red[32];
   __shared__ int s_ok;
