@@ -1180,6 +1180,8 @@ int gemm_tc(const void* x, int64_t ldx, int M, int K, const GemmSeg* segs, int n
   const int n_tiles = tc_tiles(segs, nseg, epi, starts);
   const tc::Plan pl = tc::make_plan(M, n_tiles, K, sw);
   const size_t need = tc::plan_ws_bytes(pl, sw);
+  // the cluster kernel always exchanges partials through the workspace
+  B2_CHECK_ARG(!pl.cluster || (pl.splits >= 2 && need > 0), "gemm_tc: split-K cluster plan without a workspace");
   if (need > 0) {
     B2_CHECK_ARG(ws && ws_bytes >= need, "gemm_tc: workspace of %zu bytes needed, %zu given", need, ws_bytes);
     B2_CHECK_ARG((size_t)pl.n_tiles * pl.m_tiles <= tc::kCounterSlots, "gemm_tc: too many tiles for split-K");
