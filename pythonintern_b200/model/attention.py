@@ -4,10 +4,12 @@ Drop-in for engine/model/attention.py: ``RotaryEmbedding``, ``repeat_kv`` and
 ``DistributedAttention(config, layer_idx, rank, world_size, communicator)`` with
 ``forward(x, positions, kv_pool, block_tables, is_prefill, step_id)``.
 
-The forward runs three kernels instead of the reference's per-token Python loops
-and dense gather/pad/repeat copies:
+The forward runs two or three kernels instead of the reference's per-token Python
+loops and dense gather/pad/repeat copies:
   1. ``b2_linear_qkv``: one GEMM for the q, k and v projections (attention.py:156-158);
-  2. ``b2_rope_kv_write``: RoPE on q and k and the paged K/V store (attention.py:161-184);
+  2. ``b2_rope_kv_write``: RoPE on q and k and the paged K/V store (attention.py:161-184)
+     -- for decode batches with head_dim 128 both run as one launch,
+     ``b2_linear_qkv_rope_kv``, whose GEMM epilogue rotates and stores (bit-identical);
   3. ``b2_paged_attention``: the softmax attention read straight from the pool
      through the block tables, GQA heads sharing each K/V read (attention.py:186-228);
 then the row-parallel out_proj with its all-reduce (attention.py:231-232).
