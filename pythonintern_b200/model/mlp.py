@@ -3,7 +3,8 @@
 ``gate_proj``/``up_proj`` are ColumnParallelLinear and ``down_proj`` is
 RowParallelLinear, exactly as in the reference.  The forward runs the gate and up
 GEMMs as ONE tensor-core kernel whose epilogue writes ``silu(g) * u``
-(``b2_linear_swiglu``), then the row-parallel down projection and its all-reduce.
+(``b2_linear_swiglu``; ``b2_linear_swiglu_rownorm`` when it also finishes a deferred
+RMSNorm of its input rows), then the row-parallel down projection and its all-reduce.
 """
 
 from __future__ import annotations

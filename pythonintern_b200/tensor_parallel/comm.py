@@ -16,9 +16,13 @@ Peers are connected in one of two ways:
 * one thread per GPU in one process (the reference's in-memory test harness):
   ``register_in_memory_peer`` for every peer, on distinct GPUs.
 
-The fused model path uses ``partial_buffer`` (the row-parallel GEMM writes its
-partial there) and ``allreduce_rmsnorm`` (sum + residual + next RMSNorm) without
-host synchronisation; errors then surface at the step's status check.
+The tensor-parallel decode path uses ``row_parallel_linear`` (the row-parallel GEMM
+pushes each output row to the rank that owns it from its epilogue),
+``allreduce_rmsnorm_sharded`` (sum in rank order + residual + next RMSNorm +
+all-gather, flag free) and ``argmax_allgather`` (greedy token over a vocab-parallel
+lm_head), all without host synchronisation; errors surface at the step's status
+check.  ``all_reduce_sum`` / ``allreduce_rmsnorm`` keep the reference's one-shot
+semantics for the module-level API.
 """
 
 from __future__ import annotations

@@ -1,19 +1,19 @@
 """CUDA-graph capture of the batched decode step.
 
-A decode step launches ~8 kernels per layer plus the embedding, the lm_head and the
-argmax (260 launches for 32 layers).  Launching them one by one from Python costs
-more host time than the GPU needs for a small batch, so each (batch, table width)
-bucket captures the whole step once and replays it.
+A decode step launches five kernels per decoder layer at world size 1 (seven with
+tensor parallelism) plus the embedding, the norms, the lm_head and the greedy
+sampling.  Launching them one by one from Python costs more host time than the GPU
+needs for a small batch, so each (batch, table width) bucket captures the whole step
+once and replays it.
 
 Everything the step reads that changes between steps lives in ONE static device
 buffer (token ids, positions, context lengths, padded block tables), refreshed by a
-single copy before each replay: from pinned host memory when the request comes from
-the host (``replay_host``), or from a device buffer prepared in advance
-(``replay_device``).  Kernel arguments baked into the graph (tensor maps, split
-counts, communicator buffers and call parities) stay valid because every buffer the
-step touches is either static here, part of the model, or allocated from the graph's
-private memory pool during capture.  The communicator's call parity is preserved
-across replays because a step issues an even number of all-reduces (two per layer).
+single copy from pinned host memory before each replay (``upload_host``; only the
+block-table rows that changed since the previous step are repacked).  Kernel
+arguments baked into the graph (tensor maps, split counts, communicator buffers) stay
+valid because every buffer the step touches is either static here, part of the model,
+or allocated from the graph's private memory pool during capture; the tensor-parallel
+exchange slots rotate on a device-side epoch, so replays need no host bookkeeping.
 """
 
 from __future__ import annotations
