@@ -1,32 +1,31 @@
 // Tensor-parallel all-reduce over NVLink peer memory.
 //
 // Replaces the reference's gRPC all-reduce (engine/tensor_parallel/comm.py:72-154,
-// buffer_codec.py:27-69, worker_node.py:107-125), in which every rank serialises
-// its partial tensor, sends it to every peer and sums what arrives.  Here every
-// rank owns one device allocation holding
+// buffer_codec.py:27-69, worker_node.py:107-125), in which every rank serialises its
+// partial tensor, sends it to every peer and sums what arrives.  Here every rank owns one
+// device allocation, exported once through a CUDA IPC handle:
 //
-//     [ data[0] | data[1] | flags[8][kMaxCtas] | ctrl{epoch, done} ]
+//     [ data[0] | data[1] | recv[3] | xn[3] | flags[8][kMaxCtas] | ctrl | scatter table | amx[3][8][4096] ]
 //
-// exported once through a CUDA IPC handle.  The row-parallel GEMM writes its
-// partial straight into data[parity]; the reduction kernel then
-//   1. raises flag[rank][cta] = epoch on every peer (st.release.sys),
-//   2. waits, bounded by %globaltimer, for flag[peer][cta] == epoch from every
-//      peer (ld.acquire.sys),
-//   3. loads the partial of every rank directly over NVLink and sums in rank order
-//      0..world-1 in float32 (so all ranks produce bit-identical results),
-//   4. (fused variant) adds the float32 residual, writes it back, and applies the
-//      next RMSNorm (layers.py:179-184).
-// The fused row-parallel path (b2_row_parallel_linear + b2_allreduce_rmsnorm_sharded)
-// uses no flags at all: its receive buffers rotate over three slots chosen by the device
-// epoch and are filled with a sentinel (all-ones bytes, a NaN payload that arithmetic
-// never produces) when idle, so the arrival of every element is its own signal.  A
-// slot is refilled with the sentinel one call after it was consumed, which leaves a
-// full call of slack before any rank can write it again.
-// The epoch is a device-side counter advanced by the last CTA of every call, so
-// CUDA-graph replays need no host bookkeeping.  Two data buffers alternate by call
-// parity: a rank can only start overwriting data[p] after every peer has raised
-// the flag of the following call, which it does only after finishing its reads of
-// the previous use of data[p].
+// * One-shot module API (b2_allreduce_sum / b2_allreduce_rmsnorm): the partial goes into
+//   data[parity]; each CTA raises flag[rank][cta] = epoch on every peer (st.release.sys),
+//   waits for the peers' flags with a %globaltimer bound (ld.acquire.sys), then loads every
+//   rank's partial over NVLink and sums in rank order 0..world-1 (bit-identical on all
+//   ranks); the fused variant adds the float32 residual and applies the next RMSNorm.
+//   Two data buffers alternate by call parity.
+// * Decode path (b2_row_parallel_linear + b2_allreduce_rmsnorm_sharded), flag free: the
+//   row-parallel GEMM's epilogue stores each output row into recv[b] of the rank that
+//   owns the row; the owner sums the sources in rank order, adds its float32 residual
+//   slice, normalises, and stores the row into xn[b] of every rank; every rank copies
+//   its xn[b] out.  Idle slots hold a sentinel (all-ones bytes, a NaN payload that
+//   arithmetic never produces), so the arrival of every element is its own signal; the
+//   slots rotate over three values of a device-side epoch (b = epoch % 3) and a slot is
+//   refilled with the sentinel one call after it was consumed, which leaves a full call
+//   of slack before any rank can write it again.
+// * Greedy sampling over a vocab-parallel lm_head (b2_argmax_allgather): each rank stores
+//   its (max, index) per row into amx[b] of every rank, sentinel-checked the same way.
+// Epochs advance on the device (last CTA of a call), so CUDA-graph replays need no host
+// bookkeeping; every wait is bounded and raises B2_DEV_PEER_TIMEOUT.
 #include <cstring>
 #include <new>
 
