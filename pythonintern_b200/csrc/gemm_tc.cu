@@ -7,19 +7,23 @@
 // A operand and the token tile (BN = 16..256 rows) is its B operand, giving
 // D[feature, token] = W . X^T in TMEM.  Per CTA:
 //
-//   warp 0 / lane 0 : TMA producer, STAGES-deep ring of {W 128x64, X BNx64} bf16
-//                     tiles, 128-byte swizzle, no multicast
+//   warp 0 / lane 0 : TMA producer, STAGES-deep ring of {W 128x64 (gate and up for
+//                     SwiGLU), X BNx64} bf16 tiles, 128-byte swizzle, no multicast
 //   warp 1 / lane 0 : MMA issuer, tcgen05.mma.cta_group::1.kind::f16, M=128,
 //                     N=BN, K=16 x4 per stage; tcgen05.commit frees each stage
-//   all 4 warps      : epilogue, tcgen05.ld 32x32b rows -> registers -> global
+//   epilogue warps   : tcgen05.ld 32x32b rows -> registers -> global
 //
-// Split-K over CTAs spreads skinny decode GEMMs over all SMs: every split writes
-// its float32 partial tile to the workspace, and the last split of a tile (atomic
-// counter) sums them and runs the epilogue.  Epilogues: plain store (optional
-// bias, bf16 or f32 output), grouped q|k|v segments, and SwiGLU, where each
-// 128-row A tile is 64 gate rows + the 64 matching up rows and the epilogue
-// writes silu(g) * u.  Every wait is bounded by %globaltimer; a timeout raises
-// B2_DEV_PIPE_TIMEOUT, drains the copies in flight, frees TMEM and returns.
+// Two kernels.  gemm_tc_kernel is persistent (one CTA per SM walking the tiles, TMEM
+// accumulators double-buffered so a tile's epilogue overlaps the next mainloop; a
+// uniform split-K fallback whose last CTA per tile reduces).  gemm_tc_cluster_kernel
+// splits K over a thread-block cluster of s CTAs per tile for the skinny decode GEMMs:
+// partials go through an L2 workspace and one cluster barrier, each CTA reducing 1/s of
+// the token columns.  Epilogues: plain store (optional bias, bf16 or f32 output, or the
+// reduce-scatter push of the tensor-parallel row-parallel GEMM), grouped q|k|v segments
+// (optionally with RoPE + the paged KV write), SwiGLU (gate and up accumulators in two
+// TMEM column ranges, silu(g) * u), the deferred RMSNorm producer (residual add, h * w,
+// tile sums of h^2) and consumer (row scale).  Every wait is bounded by %globaltimer; a
+// timeout raises B2_DEV_PIPE_TIMEOUT, drains the copies in flight, frees TMEM and returns.
 #include <cuda.h>
 #include <map>
 #include <mutex>
