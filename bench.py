@@ -10,6 +10,7 @@ and the KV cache is random (synthetic data; there is no checkpoint or dataset).
 
   python bench.py --gpus N --steps K --warmup W           # this framework
   python bench.py --impl reference --steps K --warmup W   # reference CPU algorithm
+  python bench.py --workload prefill                      # batched varlen prefill (below)
 
 One JSON line on rank 0:
   value        decode tokens/s with inputs resident in HBM (CUDA events, max over ranks)
@@ -20,6 +21,11 @@ One JSON line on rank 0:
   cpu_baseline the oracle restatement of the reference's CPU path on this host's
                cores, on a bounded sample (one decoder layer of a few sequences),
                extrapolated to a full step
+
+``--workload prefill`` measures the other half of a serving step instead: the
+Mistral-7B shape (vocab 32000), 16 prompts of 1024 tokens prefilled in ONE batched
+forward (the reference runs one forward per prompt), metric prefill tokens/s; the
+roofline is the dominant kernel's TFLOP/s against the bf16 tensor peak.
 """
 
 from __future__ import annotations
@@ -42,6 +48,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 HBM_FALLBACK_GBS = 6650.0
+BF16_FALLBACK_TFLOPS = 1590.0
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) over the
 # algorithmic bytes of the same launch, from one ncu capture of the attention kernel at
@@ -63,6 +70,9 @@ def parse_args(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-batch", type=int, default=4)
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode")
+    ap.add_argument("--prompts", type=int, default=16, help="prefill workload: prompts per step")
+    ap.add_argument("--prompt-len", type=int, default=1024, help="prefill workload: tokens per prompt")
     return ap.parse_args(argv)
 
 
@@ -74,6 +84,34 @@ def measured_peaks():
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return HBM_FALLBACK_GBS, "fallback"
+
+
+def measured_tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return BF16_FALLBACK_TFLOPS, "fallback"
+
+
+def init_synthetic(model, pool, seed: int, rank: int, dev):
+    """N(0, 0.02) weights (norms 1), identical replicated tensors on every rank, and a random KV cache."""
+    import torch
+    g_rep = torch.Generator(device=dev)
+    g_rep.manual_seed(seed)
+    g_shard = torch.Generator(device=dev)
+    g_shard.manual_seed(seed + 1 + rank)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if "layernorm" in name or name == "norm.weight":
+                p.fill_(1.0)
+                continue
+            replicated = name.startswith("embed_tokens") or name.startswith("lm_head")
+            p.normal_(0.0, 0.02, generator=g_rep if replicated else g_shard)
+        pool.k_cache.normal_(0.0, 1.0, generator=g_shard)
+        pool.v_cache.normal_(0.0, 1.0, generator=g_shard)
 
 
 def model_config(layers: int):
@@ -267,19 +305,7 @@ def run_ours(args):
     model, pool = engine.model, engine.kv_manager.pool
 
     # Synthetic weights: replicated tensors identical on every rank, shards per rank.
-    g_rep = torch.Generator(device=dev)
-    g_rep.manual_seed(args.seed)
-    g_shard = torch.Generator(device=dev)
-    g_shard.manual_seed(args.seed + 1 + rank)
-    with torch.no_grad():
-        for name, p in model.named_parameters():
-            if "layernorm" in name or name == "norm.weight":
-                p.fill_(1.0)
-                continue
-            replicated = name.startswith("embed_tokens") or name.startswith("lm_head")
-            p.normal_(0.0, 0.02, generator=g_rep if replicated else g_shard)
-        pool.k_cache.normal_(0.0, 1.0, generator=g_shard)
-        pool.v_cache.normal_(0.0, 1.0, generator=g_shard)
+    init_synthetic(model, pool, args.seed, rank, dev)
     perm = np.random.default_rng(args.seed).permutation(num_blocks).astype(np.int64)
     tables = [perm[b * bps:(b + 1) * bps].tolist() for b in range(B)]
 
@@ -531,10 +557,255 @@ def run_ours(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- prefill workload
+def prefill_flops(cfg, lens, world):
+    """Per rank: 2 * tokens * layer parameters + causal attention 4 * (pos + 1) * head_dim per q head."""
+    H, hd, nq, nkv, inter, L = (cfg.hidden_dim, cfg.head_dim, cfg.num_heads, cfg.num_kv_heads,
+                                cfg.intermediate_dim, cfg.num_layers)
+    params = H * (nq + 2 * nkv) * hd + nq * hd * H + 3 * H * inter
+    T = sum(lens)
+    keys = sum(P * (P + 1) // 2 for P in lens)
+    gemm = 2.0 * T * params * L / world
+    attn = 4.0 * keys * hd * nq * L / world
+    return gemm, attn
+
+
+def cpu_prefill_sample(cfg, P: int, seed: int):
+    """Oracle (numpy float32) prefill of one prompt of P tokens through one decoder layer; seconds."""
+    import oracle
+    from oracle import decoder as od
+    od.set_precision(np.float32)
+    rng = np.random.default_rng(seed)
+    H, hd, nq, nkv, inter = cfg.hidden_dim, cfg.head_dim, cfg.num_heads, cfg.num_kv_heads, cfg.intermediate_dim
+    ocfg = oracle.OracleConfig(cfg.vocab_size, H, 1, nq, nkv, inter, max(cfg.max_seq_len, P + 8), cfg.rms_norm_eps)
+    std = np.float32(0.02)
+    shard = {
+        "layers.0.input_layernorm.weight": np.ones(H, np.float32),
+        "layers.0.post_attention_layernorm.weight": np.ones(H, np.float32),
+        "layers.0.self_attn.q_proj.weight": rng.standard_normal((H, nq * hd), np.float32) * std,
+        "layers.0.self_attn.k_proj.weight": rng.standard_normal((H, nkv * hd), np.float32) * std,
+        "layers.0.self_attn.v_proj.weight": rng.standard_normal((H, nkv * hd), np.float32) * std,
+        "layers.0.self_attn.out_proj.weight": rng.standard_normal((nq * hd, H), np.float32) * std,
+        "layers.0.mlp.gate_proj.weight": rng.standard_normal((H, inter), np.float32) * std,
+        "layers.0.mlp.up_proj.weight": rng.standard_normal((H, inter), np.float32) * std,
+        "layers.0.mlp.down_proj.weight": rng.standard_normal((inter, H), np.float32) * std,
+    }
+    nb = math.ceil(P / 16)
+    pool = oracle.KVPool(1, nb, 16, nkv, hd)
+    model = oracle.OracleModel(ocfg, [shard], [pool], cos=None, sin=None)
+    h = rng.standard_normal((1, P, H), np.float32)
+    pos = np.arange(P, dtype=np.int64)[None]
+    t0 = time.perf_counter()
+    model.block(0, h, pos, [list(range(nb))], True)
+    t = time.perf_counter() - t0
+    od.set_precision(np.float64)
+    return t
+
+
+def run_prefill(args):
+    import torch
+    import torch.distributed as dist
+
+    from pythonintern_b200 import _lib, kernels, workloads
+    from pythonintern_b200.config import KVCacheConfig, ShardConfig
+    from pythonintern_b200.model.metadata import build_prefill_metadata
+    from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
+    from pythonintern_b200.worker.execution_engine import WorkerExecutionEngine
+    from pythonintern_b200.worker.messages import SequenceSlot, StepRequest
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                                device_id=dev)
+    cfg = workloads.mistral_7b_config(num_layers=args.layers)
+    n, P, W, K = args.prompts, args.prompt_len, args.warmup, args.steps
+    lens = [P] * n
+    T = sum(lens)
+    comm = None
+    if world > 1:
+        comm = DistributedCommunicator(rank, world, device=dev, max_bytes=max(64 << 20, T * cfg.hidden_dim * 2))
+        comm.connect()
+    bps = math.ceil(P / 16)
+    num_blocks = n * bps + 8
+    engine = WorkerExecutionEngine(cfg, ShardConfig(rank=rank, world_size=world),
+                                   KVCacheConfig(block_size=16, num_blocks=num_blocks, device=str(dev)), comm, dev,
+                                   max_prefill_tokens=T)
+    model, pool = engine.model, engine.kv_manager.pool
+    init_synthetic(model, pool, args.seed, rank, dev)
+    perm = np.random.default_rng(args.seed).permutation(num_blocks).astype(np.int64)
+    tables = [perm[s * bps:(s + 1) * bps].tolist() for s in range(n)]
+    prompts = np.random.default_rng(args.seed + 7).integers(0, cfg.vocab_size, size=(n, P)).astype(np.int64)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------- device-timed: prompts and metadata resident in HBM
+    md = build_prefill_metadata(lens, tables, dev)
+    ids = torch.from_numpy(prompts.reshape(1, T)).to(dev)
+
+    def step(i):
+        return model.greedy(ids, None, pool, tables, True, i, metadata=md)
+
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize(dev)
+    _lib.check_device_status(dev, "prefill warm-up")
+    barrier()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    c0 = _lib.launch_count
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(W, W + K):
+        step(i)
+    ev1.record(stream)
+    ev1.synchronize()
+    launches = _lib.launch_count - c0
+    clk = clocks.stop()
+    barrier()
+    torch.cuda.synchronize(dev)
+    _lib.check_device_status(dev, "timed prefill")
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    value = T * K / (ms / 1000.0)
+
+    # ---------------- per-kernel device time at the same token count
+    lay = model.layers
+    L = len(lay)
+    sa, ml = lay[0].self_attn, lay[0].mlp
+    nq, nkv, hd = sa.local_heads, sa.local_kv_heads, cfg.head_dim
+    H = cfg.hidden_dim
+    xn = torch.randn(T, H, device=dev).to(model.dtype)
+    q = torch.randn(T, nq * hd, device=dev).to(model.dtype)
+    attn_out = torch.empty(T, nq * hd, device=dev, dtype=model.dtype)
+    inter_in = torch.randn(T, ml.down_proj.in_features_per_partition, device=dev).to(model.dtype)
+
+    def time_calls(fn, reps):
+        fn(0)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for r in range(reps):
+            fn(r)
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps / 1000.0
+
+    gemm_f = {"qkv": 2.0 * T * H * (nq + 2 * nkv) * hd, "o_proj": 2.0 * T * nq * hd * H,
+              "gate_up_swiglu": 2.0 * T * H * 2 * ml.down_proj.in_features_per_partition,
+              "down": 2.0 * T * ml.down_proj.in_features_per_partition * H}
+    fns = {
+        "qkv": lambda r: kernels.linear_qkv(xn, lay[r % L].self_attn.q_proj.packed_weight(),
+                                            lay[r % L].self_attn.k_proj.packed_weight(),
+                                            lay[r % L].self_attn.v_proj.packed_weight()),
+        "prefill_attention": lambda r: kernels.prefill_attention(q, nq, nkv, hd, pool.k_cache, pool.v_cache, r % L,
+                                                                 md.tables, md.seq_start, md.n_seqs,
+                                                                 1.0 / math.sqrt(hd), out=attn_out),
+        "o_proj": lambda r: kernels.linear(attn_out, lay[r % L].self_attn.out_proj.packed_weight()),
+        "gate_up_swiglu": lambda r: kernels.linear_swiglu(xn, lay[r % L].mlp.gate_proj.packed_weight(),
+                                                          lay[r % L].mlp.up_proj.packed_weight()),
+        "down": lambda r: kernels.linear(inter_in, lay[r % L].mlp.down_proj.packed_weight()),
+    }
+    attn_f = 4.0 * sum(p * (p + 1) // 2 for p in lens) * hd * nq
+    kern = {}
+    for name, fn in fns.items():
+        t = time_calls(fn, 4)
+        f = attn_f if name == "prefill_attention" else gemm_f[name]
+        kern[name] = {"us": t * 1e6, "flops": f, "tflops": f / t / 1e12}
+    torch.cuda.synchronize(dev)
+    _lib.check_device_status(dev, "prefill kernel timing")
+    per_step = {k: v["us"] * L for k, v in kern.items()}
+    dominant = max(per_step, key=per_step.get)
+    peak, peak_kind = measured_tensor_peak()
+    dk = kern[dominant]
+    g_fl, a_fl = prefill_flops(cfg, lens, world)
+    roofline = {"bound": "tensor", "kernel": dominant, "achieved": dk["tflops"], "peak": peak, "unit": "TFLOP/s",
+                "frac": dk["tflops"] / peak,
+                "peak_source": ("measured (MEASURED_PEAKS.json bf16_tflops)" if peak_kind == "measured"
+                                else "fallback (1.59 PFLOP/s, an earlier cuBLAS bf16 measurement on these B200s)"),
+                "traffic": None, "algorithmic_flops_per_launch": dk["flops"],
+                "share_of_step": per_step[dominant] / 1000.0 / (ms / K),
+                "step_tflops": (g_fl + a_fl) / (ms / K / 1000.0) / 1e12}
+
+    # ---------------- end to end: StepRequests with host prompts through execute_step
+    e2e = None
+    if not args.no_e2e:
+        h2d = d2h = 0
+
+        def e2e_step(i):
+            slots = [SequenceSlot(seq_id=f"p{s}", is_prefill=True, prompt_token_ids=prompts[s].tolist(),
+                                  current_len=P, block_table=tables[s]) for s in range(n)]
+            engine.execute_step(StepRequest(step_id=i, active_sequences=slots))
+
+        for i in range(W):
+            e2e_step(i)
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(W, W + K):
+            e2e_step(i)
+            h2d, d2h = engine.last_h2d_bytes, engine.last_d2h_bytes
+        e1.record(stream)
+        e1.synchronize()
+        ms_e2e = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": T * K / (ms_e2e / 1000.0), "unit": "tokens/s", "ms_per_step": ms_e2e / K,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "api": "WorkerExecutionEngine.execute_step(StepRequest) with host prompts"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            t1 = cpu_prefill_sample(cfg, P, args.seed)
+            step_s = t1 * cfg.num_layers * n
+            cpu = {"value": T / step_s, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
+                   "sample": (f"oracle (numpy float32 restatement of the reference CPU path): one prompt of {P} "
+                              f"tokens through 1 of {cfg.num_layers} decoder layers, extrapolated to "
+                              f"{n} prompts x {cfg.num_layers} layers (the reference prefills one prompt per forward)")}
+        except Exception as e:  # pragma: no cover - reported, not fatal
+            cpu = {"value": None, "unit": "tokens/s", "error": repr(e)}
+
+    if rank == 0:
+        line = {
+            "metric": "prefill tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: N(0,0.02) weights, random prompts, random block-table permutation",
+            "config": {"workload": (f"mistral-7b-shape batched prefill, {n} prompts x {P} tokens, TP={world}"
+                                    f" ({cfg.num_layers} layers)"),
+                       "model": "mistral-7b-shape", "global_batch": n, "seq_len": P, "parallelism": f"tp{world}",
+                       "l2": "inputs larger than L2 (weights read per step >> 126 MB)"},
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
+            "gpu_launches": launches, "kernels": kern,
+        }
+        print(json.dumps(line), flush=True)
+    if comm is not None:
+        barrier()
+        comm.cleanup()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "prefill":
+        return run_prefill(args)
     return run_ours(args)
 
 

@@ -192,6 +192,24 @@ int b2_paged_attention_noalloc(const void* q, int64_t ld_q, int n_rows, int nq, 
                                float scale, void* out, int64_t ld_out, int dtype, int num_splits,
                                int32_t* status, b2_stream_t stream);
 
+/* Causal prefill attention for any number of sequences in one call.
+ * Replaces the prefill branch of DistributedAttention.forward (engine/model/attention.py:
+ * 166-174 store, :211-228 scores with the causal mask of :219-222), which the reference
+ * runs one sequence per forward (engine/worker/execution_engine.py:85-111).
+ * Rows [seq_start[s], seq_start[s+1]) of q (and out) are the tokens of sequence s, at
+ * positions seq_ctx0[s] + (row - seq_start[s]) (seq_ctx0 null: 0); row r attends to the
+ * keys at positions 0..pos(r) of its sequence, read from the pool through block-table
+ * row s (their K/V must already be stored, e.g. by b2_rope_kv_write).  seq_start must be
+ * non-decreasing with seq_start[0] >= 0 and seq_start[n_seqs] <= n_rows.
+ * bf16 only, block_size 16, head_dim 32/64/128, nq/nkv in {1,2,4,8}; other shapes return
+ * B2_ENOTSUP (the per-row b2_paged_attention covers them).  Block ids outside the pool
+ * or sequences outside [0, n_rows) set B2_DEV_RANGE in *status and are skipped. */
+int b2_prefill_attention(const void* q, int64_t ld_q, int n_rows, int nq, int nkv, int head_dim,
+                         const void* k_cache, const void* v_cache, int layer, int num_blocks, int block_size,
+                         const int32_t* block_tables, int table_stride, const int32_t* seq_start,
+                         const int32_t* seq_ctx0, int n_seqs, float scale, void* out, int64_t ld_out, int dtype,
+                         int32_t* status, b2_stream_t stream);
+
 /* ---------------------------------------------------------------- greedy sampling
  * out[r] = first index of the maximum of logits[r, 0:cols]   (execution_engine.py:103,133) */
 int b2_argmax(const float* logits, int64_t ld, int rows, int cols, int64_t* out, b2_stream_t stream);

@@ -532,6 +532,269 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnP
   attn_finalize<__nv_bfloat16, HD, REP>(p, sm_m, sm_l, sm_acc, kMmaWarps, row, g, split, ctx);
 }
 
+// ---------------------------------------------------------------------------------------
+// Causal varlen prefill attention (bf16, mma.sync m16n8k16 over the paged pool).
+//
+// engine/model/attention.py:166-174 and :211-228 for a prefill: every prompt token
+// attends to the keys of its own sequence at positions 0..pos (the causal mask of
+// :219-222).  The reference runs one sequence per forward (execution_engine.py:85-111);
+// here any number of sequences of any lengths go in one launch.  Rows
+// [seq_start[s], seq_start[s+1]) are the tokens of sequence s, at positions
+// seq_ctx0[s] + (row - seq_start[s]); their K/V are already in the pool, reached
+// through block-table row s.
+//
+// A CTA owns one kv head and a tile of QT = 64 / REP consecutive tokens of one sequence.
+// Its 64 MMA rows are the (token, query head) pairs of the tile that share the kv head
+// (row m = token * REP + head), so each K/V block staged in shared memory serves QT
+// tokens x REP heads, against REP heads of one token in the decode kernel.  The 4 warps
+// (16 rows each) walk blocks 0..(last position of the tile) / 16 together through a
+// kPfStages-deep cp.async ring; a warp skips the blocks that lie wholly after all of its
+// rows.  Per row, online softmax in the log2 domain; a row's result depends only on its
+// own keys and their block order, not on which other rows share its tile.
+struct PrefillParams {
+  const void* q;
+  int64_t ld_q;
+  int n_rows, nq, nkv;
+  const void* k_cache;
+  const void* v_cache;
+  int64_t layer_off;  // elements
+  int num_blocks;
+  const int32_t* tables;
+  int table_stride;
+  const int32_t* seq_start;  // [n_seqs + 1], non-decreasing, within [0, n_rows]
+  const int32_t* seq_ctx0;   // [n_seqs] keys already cached before the first row, or null (0)
+  int n_seqs;
+  float scale_log2;
+  void* out;
+  int64_t ld_out;
+  int32_t* status;
+};
+
+constexpr int kPfWarps = 4;
+constexpr int kPfRows = kPfWarps * 16;  // MMA rows per CTA
+constexpr int kPfStages = 4;
+
+template <int HD>
+struct PfCfg {
+  static constexpr size_t SMEM = (size_t)kPfStages * MmaCfg<HD>::STAGEB;
+};
+
+// Upper bound on the CTAs along x: sum_s ceil(len_s / QT) <= n_rows / QT + n_seqs.
+static inline int prefill_tiles_bound(int n_rows, int n_seqs, int qt) { return n_rows / qt + n_seqs; }
+
+template <int HD, int REP>
+__global__ void __launch_bounds__(kPfWarps * 32) prefill_attn_mma_kernel(PrefillParams p) {
+  pdl_wait();
+  pdl_trigger();
+  using C = MmaCfg<HD>;
+  static_assert(kPfRows % REP == 0, "tile rows must hold whole tokens");
+  constexpr int QT = kPfRows / REP;  // tokens per tile
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int g = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int qr = lane >> 2, qt = lane & 3;
+
+  // (sequence, tile) of this CTA.  Tiles are numbered sequence by sequence, each
+  // sequence's last (longest) tile first; every warp finds the same answer.
+  int seq = -1, tile = 0;
+  {
+    int base = 0;
+    for (int s0 = 0; s0 < p.n_seqs && seq < 0; s0 += 32) {
+      const int s = s0 + lane;
+      int nt = 0;
+      if (s < p.n_seqs) {
+        const int len = p.seq_start[s + 1] - p.seq_start[s];
+        nt = len > 0 ? (len + QT - 1) / QT : 0;
+      }
+      int inc = nt;  // inclusive prefix sum over the lanes
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += v;
+      }
+      const int total = __shfl_sync(0xffffffffu, inc, 31);
+      const int bx = (int)blockIdx.x - base;
+      if (bx < total) {  // warp-uniform
+        const unsigned hit = __ballot_sync(0xffffffffu, bx < inc);
+        const int l = __ffs(hit) - 1;
+        const int inc_l = __shfl_sync(0xffffffffu, inc, l);
+        const int nt_l = __shfl_sync(0xffffffffu, nt, l);
+        seq = s0 + l;
+        tile = bx - (inc_l - nt_l);
+      }
+      base += total;
+    }
+  }
+  if (seq < 0) return;  // past the last tile (the grid is an upper bound)
+  const int rs = p.seq_start[seq], re = p.seq_start[seq + 1];
+  const int ctx0 = p.seq_ctx0 ? p.seq_ctx0[seq] : 0;
+  if (rs < 0 || re > p.n_rows || ctx0 < 0) {
+    if (threadIdx.x == 0) raise_status(p.status, B2_DEV_RANGE);
+    return;
+  }
+  const int len = re - rs;
+  const int ntile = (len + QT - 1) / QT;
+  const int t0 = (ntile - 1 - tile) * QT;  // first token of the tile within its sequence
+  const int nt = min(QT, len - t0);        // tokens in the tile (>= 1)
+  const int nblk = (ctx0 + t0 + nt - 1) / 16 + 1;
+  const int32_t* table = p.tables + (int64_t)seq * p.table_stride;
+
+  // This lane's two MMA rows (qr and qr + 8 of the warp's 16).
+  const int m_lo = warp * 16 + qr, m_hi = m_lo + 8;
+  const int tk_lo = m_lo / REP, tk_hi = m_hi / REP;
+  const bool ok_lo = tk_lo < nt, ok_hi = tk_hi < nt;
+  const int pos_lo = ctx0 + t0 + tk_lo, pos_hi = ctx0 + t0 + tk_hi;
+  const int64_t row_lo = rs + t0 + tk_lo, row_hi = rs + t0 + tk_hi;
+  const int col_lo = (g * REP + m_lo % REP) * HD, col_hi = (g * REP + m_hi % REP) * HD;
+  // Last position any row of this warp attends to (warp-uniform).
+  const int wpos = ctx0 + t0 + min(nt - 1, (warp * 16 + 15) / REP);
+
+  // Q fragments: a0/a2 = row qr (k lo/hi), a1/a3 = row qr + 8.
+  uint32_t qa[HD / 16][4];
+  {
+    const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(p.q);
+    const __nv_bfloat16* qlo = ok_lo ? qb + row_lo * p.ld_q + col_lo : nullptr;
+    const __nv_bfloat16* qhi = ok_hi ? qb + row_hi * p.ld_q + col_hi : nullptr;
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      qa[kk][0] = ok_lo ? *reinterpret_cast<const uint32_t*>(qlo + kk * 16 + 2 * qt) : 0u;
+      qa[kk][1] = ok_hi ? *reinterpret_cast<const uint32_t*>(qhi + kk * 16 + 2 * qt) : 0u;
+      qa[kk][2] = ok_lo ? *reinterpret_cast<const uint32_t*>(qlo + kk * 16 + 8 + 2 * qt) : 0u;
+      qa[kk][3] = ok_hi ? *reinterpret_cast<const uint32_t*>(qhi + kk * 16 + 8 + 2 * qt) : 0u;
+    }
+  }
+
+  const int64_t tok_stride_b = (int64_t)p.nkv * HD * 2;
+  const char* kbase = reinterpret_cast<const char*>(p.k_cache) + (p.layer_off + (int64_t)g * HD) * 2;
+  const char* vbase = reinterpret_cast<const char*>(p.v_cache) + (p.layer_off + (int64_t)g * HD) * 2;
+  const uint32_t sbase = smem_addr(smem);
+
+  auto block_id = [&](int b) -> int { return b < p.table_stride ? table[b] : -1; };
+  // All threads copy block b (K and V rows of this kv head) into ring slot b % kPfStages;
+  // a block id outside the pool is not read (its scores are masked).
+  auto issue = [&](int b) {
+    const int blk = block_id(b);
+    if (blk < 0 || blk >= p.num_blocks) return;
+    const uint32_t st = sbase + (uint32_t)((b % kPfStages) * C::STAGEB);
+    const int64_t blk_off = (int64_t)blk * 16 * tok_stride_b;
+    for (int i = threadIdx.x; i < 16 * C::CHUNKS; i += kPfWarps * 32) {
+      const int r = i / C::CHUNKS, c = i % C::CHUNKS;
+      const int64_t src = blk_off + r * tok_stride_b + c * 16;
+      cp_async16(st + swz<HD>(r, c), kbase + src);
+      cp_async16(st + C::BLKB + swz<HD>(r, c), vbase + src);
+    }
+  };
+
+  float o[HD / 8][4];
+#pragma unroll
+  for (int d = 0; d < HD / 8; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
+  float m_lo_run = -INFINITY, m_hi_run = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+
+#pragma unroll
+  for (int i = 0; i < kPfStages - 1; ++i) {
+    if (i < nblk) issue(i);
+    cp_async_commit();
+  }
+  for (int b = 0; b < nblk; ++b) {
+    cp_async_wait<kPfStages - 2>();  // block b has landed (this thread's copies) ...
+    __syncthreads();                 // ... for every thread, and slot (b - 1) is free
+    if (b + kPfStages - 1 < nblk) issue(b + kPfStages - 1);
+    cp_async_commit();
+    const int blk = block_id(b);
+    const bool blk_ok = blk >= 0 && blk < p.num_blocks;
+    if (!blk_ok && threadIdx.x == 0) raise_status(p.status, B2_DEV_RANGE);
+    if (b * 16 > wpos) continue;  // every key of the block follows every row of this warp
+    const uint32_t ks = sbase + (uint32_t)((b % kPfStages) * C::STAGEB);
+    const uint32_t vs = ks + C::BLKB;
+
+    // S = Q K^T over the block's 16 keys: two 8-key n-tiles.
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      const int mrow = (lane & 7) + ((lane >> 4) << 3);
+      const int mchunk = kk * 2 + ((lane >> 3) & 1);
+      uint32_t bf[4];
+      ldsm_x4(ks + swz<HD>(mrow, mchunk), bf);
+      mma_bf16(s[0], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], bf[0], bf[1]);
+      mma_bf16(s[1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], bf[2], bf[3]);
+    }
+    // Scale, causal mask, online softmax for rows qr (elements 0, 1) and qr + 8 (2, 3).
+    const int kb = b * 16;
+    float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = kb + j * 8 + 2 * qt + e;
+        const float vlo = (blk_ok && ok_lo && t <= pos_lo) ? s[j][e] * p.scale_log2 : -INFINITY;
+        const float vhi = (blk_ok && ok_hi && t <= pos_hi) ? s[j][2 + e] * p.scale_log2 : -INFINITY;
+        s[j][e] = vlo;
+        s[j][2 + e] = vhi;
+        mx_lo = fmaxf(mx_lo, vlo);
+        mx_hi = fmaxf(mx_hi, vhi);
+      }
+    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+    const float mn_lo = fmaxf(m_lo_run, mx_lo), mn_hi = fmaxf(m_hi_run, mx_hi);
+    const float c_lo = safe_exp2_diff(m_lo_run, mn_lo), c_hi = safe_exp2_diff(m_hi_run, mn_hi);
+    float pv[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        pv[j][e] = mn_lo == -INFINITY ? 0.f : safe_exp2_diff(s[j][e], mn_lo);
+        pv[j][2 + e] = mn_hi == -INFINITY ? 0.f : safe_exp2_diff(s[j][2 + e], mn_hi);
+      }
+    l_lo = l_lo * c_lo + (pv[0][0] + pv[0][1] + pv[1][0] + pv[1][1]);
+    l_hi = l_hi * c_hi + (pv[0][2] + pv[0][3] + pv[1][2] + pv[1][3]);
+    m_lo_run = mn_lo;
+    m_hi_run = mn_hi;
+#pragma unroll
+    for (int d = 0; d < HD / 8; ++d) {
+      o[d][0] *= c_lo;
+      o[d][1] *= c_lo;
+      o[d][2] *= c_hi;
+      o[d][3] *= c_hi;
+    }
+    // P (bf16) as the A operand: a0/a2 = row qr keys lo/hi, a1/a3 = row qr + 8.
+    const uint32_t pa0 = pack_bf16(pv[0][0], pv[0][1]);
+    const uint32_t pa1 = pack_bf16(pv[0][2], pv[0][3]);
+    const uint32_t pa2 = pack_bf16(pv[1][0], pv[1][1]);
+    const uint32_t pa3 = pack_bf16(pv[1][2], pv[1][3]);
+#pragma unroll
+    for (int d = 0; d < HD / 8; d += 2) {
+      const int mrow = (lane & 7) + (((lane >> 3) & 1) << 3);
+      const int mchunk = d + (lane >> 4);
+      uint32_t bf[4];
+      ldsm_x4_trans(vs + swz<HD>(mrow, mchunk), bf);
+      mma_bf16(o[d], pa0, pa1, pa2, pa3, bf[0], bf[1]);
+      mma_bf16(o[d + 1], pa0, pa1, pa2, pa3, bf[2], bf[3]);
+    }
+  }
+  cp_async_wait<0>();
+  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+  __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(p.out);
+  if (ok_lo) {
+    __nv_bfloat16* dst = ob + row_lo * p.ld_out + col_lo + 2 * qt;
+#pragma unroll
+    for (int d = 0; d < HD / 8; ++d)
+      *reinterpret_cast<uint32_t*>(dst + d * 8) =
+          pack_bf16(l_lo > 0.f ? o[d][0] / l_lo : 0.f, l_lo > 0.f ? o[d][1] / l_lo : 0.f);
+  }
+  if (ok_hi) {
+    __nv_bfloat16* dst = ob + row_hi * p.ld_out + col_hi + 2 * qt;
+#pragma unroll
+    for (int d = 0; d < HD / 8; ++d)
+      *reinterpret_cast<uint32_t*>(dst + d * 8) =
+          pack_bf16(l_hi > 0.f ? o[d][2] / l_hi : 0.f, l_hi > 0.f ? o[d][3] / l_hi : 0.f);
+  }
+}
+
 // Opts a kernel into `bytes` of dynamic shared memory once per (kernel, device).
 static int allow_dynamic_smem(const void* fn, size_t bytes) {
   static std::mutex mu;
@@ -569,6 +832,24 @@ static int launch_mma(int hd, int rep, const AttnParams& p, dim3 grid, cudaStrea
     case 64: return launch_mma_rep<64>(rep, p, grid, s);
     case 128: return launch_mma_rep<128>(rep, p, grid, s);
     default: return fail(B2_ENOTSUP, "b2_paged_attention: bf16 head_dim %d not supported (32, 64, 128)", hd);
+  }
+}
+
+template <int HD>
+static int launch_prefill_rep(int rep, int n_rows, const PrefillParams& p, cudaStream_t s) {
+  auto go = [&](void (*k)(PrefillParams), int qt) -> int {
+    const int rc = allow_dynamic_smem((const void*)k, PfCfg<HD>::SMEM);
+    if (rc) return rc;
+    const dim3 grid(prefill_tiles_bound(n_rows, p.n_seqs, qt), p.nkv);
+    B2_TRY_CUDA(launch_pdl(k, grid, dim3(kPfWarps * 32), PfCfg<HD>::SMEM, s, p));
+    return B2_OK;
+  };
+  switch (rep) {
+    case 1: return go(prefill_attn_mma_kernel<HD, 1>, kPfRows / 1);
+    case 2: return go(prefill_attn_mma_kernel<HD, 2>, kPfRows / 2);
+    case 4: return go(prefill_attn_mma_kernel<HD, 4>, kPfRows / 4);
+    case 8: return go(prefill_attn_mma_kernel<HD, 8>, kPfRows / 8);
+    default: return fail(B2_ENOTSUP, "b2_prefill_attention: nq/nkv = %d not supported (1, 2, 4, 8)", rep);
   }
 }
 
@@ -737,6 +1018,54 @@ int b2_paged_attention_noalloc(const void* q, int64_t ld_q, int n_rows, int nq, 
   return b2_paged_attention(q, ld_q, n_rows, nq, nkv, head_dim, k_cache, v_cache, layer, num_blocks, block_size,
                             block_tables, table_stride, table_index, ctx_lens, compat_pad, scale, out, ld_out,
                             dtype, scratch, scratch ? b2::kNoAllocScratchBytes : 0, num_splits, status, stream);
+}
+
+
+int b2_prefill_attention(const void* q, int64_t ld_q, int n_rows, int nq, int nkv, int head_dim,
+                         const void* k_cache, const void* v_cache, int layer, int num_blocks, int block_size,
+                         const int32_t* block_tables, int table_stride, const int32_t* seq_start,
+                         const int32_t* seq_ctx0, int n_seqs, float scale, void* out, int64_t ld_out, int dtype,
+                         int32_t* status, b2_stream_t stream) {
+  B2_CHECK_ARG(n_rows >= 0 && n_seqs >= 0 && nq > 0 && nkv > 0 && nq % nkv == 0,
+               "b2_prefill_attention: bad sizes");
+  B2_CHECK_ARG(dtype == B2_BF16, "b2_prefill_attention: bf16 only (float32 prefill runs b2_paged_attention)");
+  B2_CHECK_ARG(block_size == 16, "b2_prefill_attention: block_size %d (16 only)", block_size);
+  B2_CHECK_ARG(num_blocks > 0 && table_stride > 0 && layer >= 0, "b2_prefill_attention: bad cache geometry");
+  B2_CHECK_ARG(ld_q >= (int64_t)nq * head_dim && ld_out >= (int64_t)nq * head_dim,
+               "b2_prefill_attention: row strides too small");
+  B2_CHECK_ARG(nkv <= 65535, "b2_prefill_attention: nkv %d > 65535", nkv);
+  if (n_rows == 0 || n_seqs == 0) return B2_OK;
+  B2_CHECK_ARG(q && k_cache && v_cache && block_tables && seq_start && out && status,
+               "b2_prefill_attention: null pointer");
+  B2_CHECK_ARG(((uintptr_t)q % 4) == 0 && (ld_q % 2) == 0 && ((uintptr_t)out % 4) == 0 && (ld_out % 2) == 0 &&
+                   ((uintptr_t)k_cache % 16) == 0 && ((uintptr_t)v_cache % 16) == 0,
+               "b2_prefill_attention: q/out need 4-byte rows, the cache 16-byte alignment");
+  b2::PrefillParams p{};
+  p.q = q;
+  p.ld_q = ld_q;
+  p.n_rows = n_rows;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.layer_off = (int64_t)layer * num_blocks * block_size * nkv * head_dim;
+  p.num_blocks = num_blocks;
+  p.tables = block_tables;
+  p.table_stride = table_stride;
+  p.seq_start = seq_start;
+  p.seq_ctx0 = seq_ctx0;
+  p.n_seqs = n_seqs;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = out;
+  p.ld_out = ld_out;
+  p.status = status;
+  const int rep = nq / nkv;
+  switch (head_dim) {
+    case 32: return b2::launch_prefill_rep<32>(rep, n_rows, p, stream);
+    case 64: return b2::launch_prefill_rep<64>(rep, n_rows, p, stream);
+    case 128: return b2::launch_prefill_rep<128>(rep, n_rows, p, stream);
+    default: return b2::fail(B2_ENOTSUP, "b2_prefill_attention: head_dim %d not supported (32, 64, 128)", head_dim);
+  }
 }
 
 }  // extern "C"

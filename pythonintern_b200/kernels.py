@@ -293,6 +293,37 @@ def paged_attention(q: torch.Tensor, nq: int, nkv: int, head_dim: int, k_cache: 
     return out
 
 
+def prefill_supported(dtype: torch.dtype, nq: int, nkv: int, head_dim: int, block_size: int) -> bool:
+    """Shapes ``b2_prefill_attention`` runs (the per-row ``paged_attention`` covers the rest)."""
+    return (dtype == torch.bfloat16 and block_size == 16 and head_dim in (32, 64, 128)
+            and nq % nkv == 0 and nq // nkv in (1, 2, 4, 8))
+
+
+def prefill_attention(q: torch.Tensor, nq: int, nkv: int, head_dim: int, k_cache: torch.Tensor,
+                      v_cache: torch.Tensor, layer: int, block_tables: torch.Tensor, seq_start: torch.Tensor,
+                      n_seqs: int, scale: float, seq_ctx0: Optional[torch.Tensor] = None,
+                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal attention of every prompt token of ``n_seqs`` sequences in one launch.
+
+    Rows ``[seq_start[s], seq_start[s+1])`` of ``q`` are sequence s at positions
+    ``seq_ctx0[s] + (row - seq_start[s])``; each attends to keys ``0..pos`` of its own
+    sequence in the pool (block-table row s).  engine/model/attention.py:166-174,211-228,
+    which the reference runs one sequence at a time (execution_engine.py:85-111).
+    """
+    n_rows = q.shape[0]
+    _, NB, bs, _, _ = k_cache.shape
+    if out is None:
+        out = torch.empty(n_rows, nq * head_dim, dtype=q.dtype, device=q.device)
+    assert seq_start.dtype == torch.int32 and seq_start.numel() >= n_seqs + 1
+    assert seq_ctx0 is None or (seq_ctx0.dtype == torch.int32 and seq_ctx0.numel() >= n_seqs)
+    check(_lib.lib().b2_prefill_attention(
+        ptr(q), q.stride(0), n_rows, nq, nkv, head_dim, ptr(k_cache), ptr(v_cache), layer, NB, bs,
+        ptr(block_tables), block_tables.shape[1], ptr(seq_start), ptr(seq_ctx0), n_seqs, float(scale),
+        ptr(out), out.stride(0), dtype_code(q.dtype), status_ptr(q.device), stream_ptr(q.device)),
+        "b2_prefill_attention")
+    return out
+
+
 def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """First index of each row's maximum (engine/worker/execution_engine.py:103,133)."""
     assert logits.dtype == torch.float32 and logits.dim() == 2 and logits.stride(1) == 1

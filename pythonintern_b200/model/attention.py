@@ -12,6 +12,9 @@ loops and dense gather/pad/repeat copies:
      ``b2_linear_qkv_rope_kv``, whose GEMM epilogue rotates and stores (bit-identical);
   3. ``b2_paged_attention``: the softmax attention read straight from the pool
      through the block tables, GQA heads sharing each K/V read (attention.py:186-228);
+     a bf16 prefill runs ``b2_prefill_attention`` instead, every prompt token of every
+     sequence of the call in one causal launch that shares each K/V block across a tile
+     of tokens (attention.py:166-174,211-228);
 then the row-parallel out_proj with its all-reduce (attention.py:231-232).
 """
 
@@ -140,6 +143,12 @@ class DistributedAttention(nn.Module):
             kernels.rope_kv_write(qkv, nq, nkv, hd, md.rope_pos, md.store_pos, md.table_index, md.tables,
                                   self.rope.cos_cached, self.rope.sin_cached, q, pool.k_cache, pool.v_cache,
                                   self.layer_idx)
+        if (md.is_prefill and md.seq_start is not None
+                and kernels.prefill_supported(wdt, nq, nkv, hd, pool.block_size)):
+            # every prompt token of every sequence in one causal launch
+            return kernels.prefill_attention(q, nq, nkv, hd, pool.k_cache, pool.v_cache, self.layer_idx, md.tables,
+                                             md.seq_start, md.n_seqs, 1.0 / math.sqrt(hd), seq_ctx0=md.seq_ctx0,
+                                             out=out)
         splits = kernels.attention_splits(md.n_tokens, nkv, md.max_ctx, pool.block_size, x2d.device)
         return kernels.paged_attention(q, nq, nkv, hd, pool.k_cache, pool.v_cache, self.layer_idx, md.tables,
                                        md.table_index, md.ctx_lens, md.compat_pad, 1.0 / math.sqrt(hd),

@@ -218,7 +218,10 @@ class DistributedLLaMAModel(nn.Module):
             md = metadata or build_metadata(positions, block_tables, is_prefill, self.device,
                                             masked_padding=self.config.masked_decode_padding)
             xn = self.forward_hidden(token_ids, md, kv_pool)
-            last = xn.view(B, S, -1)[:, -1, :]  # row-strided view, no copy
+            if md.last_rows is not None:  # varlen prefill: gather each sequence's last row
+                last = kernels.embedding(md.last_rows, xn)
+            else:
+                last = xn.view(B, S, -1)[:, -1, :]  # row-strided view, no copy
             w = self.lm_head.weight
             if self.world_size == 1:
                 logits = kernels.linear(last, w, out_dtype=torch.float32)
@@ -245,6 +248,9 @@ class DistributedLLaMAModel(nn.Module):
                                             masked_padding=self.config.masked_decode_padding)
             xn = self.forward_hidden(token_ids, md, kv_pool, trace=trace)
             if return_logits_last_only:
-                last = xn.view(B, S, -1)[:, -1, :]  # row-strided view, no copy
+                if md.last_rows is not None:
+                    last = kernels.embedding(md.last_rows, xn)
+                else:
+                    last = xn.view(B, S, -1)[:, -1, :]  # row-strided view, no copy
                 return kernels.linear(last, self.lm_head.weight, out_dtype=torch.float32)
             return kernels.linear(xn, self.lm_head.weight, out_dtype=torch.float32).view(B, S, -1)

@@ -11,6 +11,9 @@ device arrays, built on the host with numpy and copied in one go:
   token (b, t) is rotated at ``positions[b, t]``, stored at logical slot ``t``
   (attention.py:168-173) and attends causally to slots ``0..t``
   (attention.py:219-222), i.e. ``ctx = t + 1`` without padding.
+* varlen prefill (``build_prefill_metadata``): the prompts of several sequences of
+  different lengths concatenated into one call; ``seq_start`` delimits them and
+  ``last_rows`` picks each sequence's last token for the lm_head.
 """
 
 from __future__ import annotations
@@ -33,6 +36,13 @@ class TokenMetadata:
     ctx_lens: torch.Tensor            # int32 [T]
     max_ctx: int
     compat_pad: bool
+    # Prefill only: rows [seq_start[s], seq_start[s+1]) are sequence s (int32 [n_seqs + 1]),
+    # at positions seq_ctx0[s] + (row - seq_start[s]) (seq_ctx0 None: 0).
+    seq_start: Optional[torch.Tensor] = None
+    n_seqs: int = 0
+    seq_ctx0: Optional[torch.Tensor] = None
+    # Varlen prefill: the row of each sequence's last token (int64 [n_seqs]).
+    last_rows: Optional[torch.Tensor] = None
 
 
 def pad_tables(block_tables: Sequence[Sequence[int]], min_width: int = 1) -> np.ndarray:
@@ -117,12 +127,14 @@ def build_metadata(positions, block_tables: Sequence[Sequence[int]], is_prefill:
         pos = pos[:, None]
     B, S = pos.shape
     tables = pad_tables(block_tables)
+    seq_start = None
     if is_prefill:
         store = np.tile(np.arange(S, dtype=np.int64), B)
         tidx = np.repeat(np.arange(B, dtype=np.int32), S)
         ctx = (store + 1).astype(np.int32)
         rope = pos.reshape(-1)
         compat = False
+        seq_start = (np.arange(B + 1, dtype=np.int32) * S).astype(np.int32)
     else:
         assert S == 1, "decode takes one token per sequence"
         rope = pos[:, 0]
@@ -132,12 +144,60 @@ def build_metadata(positions, block_tables: Sequence[Sequence[int]], is_prefill:
         compat = not masked_padding
     dev = torch.device(device)
     arrays = [rope.astype(np.int64), None if store is None else store.astype(np.int64), tidx, tables,
-              ctx, extra]
+              ctx, extra, seq_start]
     if stager is not None:
         d = stager.upload(arrays)
     else:
         d = [None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(dev) for a in arrays]
     md = TokenMetadata(n_tokens=B * S, is_prefill=is_prefill, rope_pos=d[0], store_pos=d[1], table_index=d[2],
-                       tables=d[3], ctx_lens=d[4], max_ctx=int(ctx.max()) if ctx.size else 0, compat_pad=compat)
+                       tables=d[3], ctx_lens=d[4], max_ctx=int(ctx.max()) if ctx.size else 0, compat_pad=compat,
+                       seq_start=d[6], n_seqs=B if is_prefill else 0)
+    md.extra = d[5]
+    return md
+
+
+def prefill_layout(prompt_lens: Sequence[int], ctx0: Optional[Sequence[int]] = None):
+    """Host arrays of a varlen prefill: (rope/store positions int64 [T], table row int32 [T],
+    ctx int32 [T], seq_start int32 [n+1], last rows int64 [n], ctx0 int32 [n] or None)."""
+    lens = np.asarray(prompt_lens, dtype=np.int64).reshape(-1)
+    if lens.size == 0 or (lens <= 0).any():
+        raise ValueError(f"varlen prefill needs prompts of at least one token, got lengths {lens.tolist()}")
+    n = lens.size
+    c0 = np.zeros(n, dtype=np.int64) if ctx0 is None else np.asarray(ctx0, dtype=np.int64).reshape(n)
+    if (c0 < 0).any():
+        raise ValueError("seq_ctx0 must be >= 0")
+    seq_start = np.zeros(n + 1, dtype=np.int64)
+    np.cumsum(lens, out=seq_start[1:])
+    T = int(seq_start[-1])
+    tidx = np.repeat(np.arange(n, dtype=np.int32), lens)
+    pos = np.arange(T, dtype=np.int64) - np.repeat(seq_start[:-1], lens) + np.repeat(c0, lens)
+    ctx = (pos + 1).astype(np.int32)
+    last = (seq_start[1:] - 1).astype(np.int64)
+    return pos, tidx, ctx, seq_start.astype(np.int32), last, (None if ctx0 is None else c0.astype(np.int32))
+
+
+def build_prefill_metadata(prompt_lens: Sequence[int], block_tables: Sequence[Sequence[int]], device,
+                           stager: Optional[PinnedStager] = None, extra=None,
+                           ctx0: Optional[Sequence[int]] = None) -> TokenMetadata:
+    """Metadata of one prefill call over several prompts of different lengths.
+
+    Sequence s contributes ``prompt_lens[s]`` consecutive rows at positions
+    ``ctx0[s] + arange(prompt_lens[s])`` (the reference's ``arange(P)`` when ctx0 is
+    None, execution_engine.py:88-93), stored through block-table row s.  ``extra``
+    (e.g. the concatenated token ids) rides along in the same upload.
+    """
+    if len(block_tables) != len(prompt_lens):
+        raise ValueError(f"{len(block_tables)} block tables for {len(prompt_lens)} prompts")
+    pos, tidx, ctx, seq_start, last, c0 = prefill_layout(prompt_lens, ctx0)
+    tables = pad_tables(block_tables)
+    arrays = [pos, None, tidx, tables, ctx, extra, seq_start, last, c0]
+    if stager is not None:
+        d = stager.upload(arrays)
+    else:
+        dev = torch.device(device)
+        d = [None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(dev) for a in arrays]
+    md = TokenMetadata(n_tokens=int(pos.size), is_prefill=True, rope_pos=d[0], store_pos=d[0], table_index=d[2],
+                       tables=d[3], ctx_lens=d[4], max_ctx=int(ctx.max()), compat_pad=False, seq_start=d[6],
+                       n_seqs=len(prompt_lens), seq_ctx0=d[8], last_rows=d[7])
     md.extra = d[5]
     return md

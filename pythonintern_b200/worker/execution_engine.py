@@ -2,14 +2,18 @@
 
 ``WorkerExecutionEngine(model_config, shard_config, kv_config, communicator,
 device).execute_step(step_request)`` keeps the reference's semantics: each
-prefill runs as its own batch-1 forward with positions ``arange(P)``; all decodes
-run as one batch with positions ``current_len - 1``; the sampled token is the
-rank-local greedy argmax and ``top_logits`` the first ten logits of the row.
+prefill sequence is computed at positions ``arange(P)`` and attends causally to its
+own tokens only; all decodes run as one batch with positions ``current_len - 1``;
+the sampled token is the rank-local greedy argmax and ``top_logits`` the first ten
+logits of the row.
 
 What changes is where the work runs: the model is the fused CUDA path, the
 argmax is a kernel, and the whole step costs one host synchronisation (one
 device-to-host copy of every sampled token and its ten logits, plus the kernel
-status word).
+status word).  The reference runs one forward per prefill sequence
+(execution_engine.py:85-111); here the step's prompts are concatenated into as few
+forwards as the token cap allows (``batch_prefills``), so the weights are read once
+for all of them and the attention is one varlen causal launch per layer.
 """
 
 from __future__ import annotations
@@ -24,7 +28,7 @@ from pythonintern_b200 import _lib
 from pythonintern_b200.config import KVCacheConfig, ModelConfig, ShardConfig
 from pythonintern_b200.model.kv_cache import KVCacheManager
 from pythonintern_b200.model.llama import DistributedLLaMAModel
-from pythonintern_b200.model.metadata import PinnedStager, build_metadata
+from pythonintern_b200.model.metadata import PinnedStager, build_metadata, build_prefill_metadata
 from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
 from pythonintern_b200.worker.graphs import DecodeGraphCache
 from pythonintern_b200.worker.messages import SampledToken, StepResponse
@@ -33,7 +37,8 @@ from pythonintern_b200.worker.messages import SampledToken, StepResponse
 class WorkerExecutionEngine:
     def __init__(self, model_config: ModelConfig, shard_config: ShardConfig, kv_config: KVCacheConfig,
                  communicator: Optional[DistributedCommunicator] = None, device="cuda",
-                 use_cuda_graphs: bool = True):
+                 use_cuda_graphs: bool = True, batch_prefills: bool = True,
+                 max_prefill_tokens: Optional[int] = None):
         self.model_config = model_config
         self.shard_config = shard_config
         self.kv_config = kv_config
@@ -50,6 +55,15 @@ class WorkerExecutionEngine:
                                            world_size=shard_config.world_size, communicator=communicator, device=dev)
         self.stager = PinnedStager(dev)
         self.use_cuda_graphs = use_cuda_graphs
+        self.batch_prefills = batch_prefills
+        if max_prefill_tokens is None:
+            max_prefill_tokens = 16384
+            if shard_config.world_size > 1 and communicator is not None:
+                # a row-parallel partial [tokens, hidden] must fit the communicator's buffer
+                esz = torch.tensor([], dtype=self.model.dtype).element_size()
+                max_prefill_tokens = min(max_prefill_tokens,
+                                         communicator.max_bytes // (model_config.hidden_dim * esz))
+        self.max_prefill_tokens = max(1, int(max_prefill_tokens))
         self.graphs = DecodeGraphCache(self.model, self.kv_manager.pool, model_config.masked_decode_padding)
         self._pin_tok: Optional[torch.Tensor] = None  # pinned read-back buffers (_read_back)
         self._pin_top: Optional[torch.Tensor] = None
@@ -82,6 +96,23 @@ class WorkerExecutionEngine:
             _lib.raise_for_status(v, f"step {step_id}")
         return self._pin_tok[:n].numpy(), self._pin_top[:n].numpy()
 
+    def _prefill_groups(self, slots) -> List[list]:
+        """Consecutive prefill slots packed into groups of at most ``max_prefill_tokens``
+        prompt tokens (a longer prompt forms a group of its own)."""
+        if not self.batch_prefills:
+            return [[s] for s in slots]
+        groups, cur, n = [], [], 0
+        for s in slots:
+            P = len(s.prompt_token_ids)
+            if cur and n + P > self.max_prefill_tokens:
+                groups.append(cur)
+                cur, n = [], 0
+            cur.append(s)
+            n += P
+        if cur:
+            groups.append(cur)
+        return groups
+
     def execute_step(self, step_request) -> StepResponse:
         start = time.perf_counter()
         step_id = step_request.step_id
@@ -93,17 +124,17 @@ class WorkerExecutionEngine:
         ids: List[str] = []
         h2d = 0
         with torch.no_grad(), torch.cuda.device(self.device):
-            for slot in prefill_slots:
-                prompt = np.asarray([list(slot.prompt_token_ids)], dtype=np.int64)
-                P = prompt.shape[1]
-                table = [list(slot.block_table)]
-                md = build_metadata(np.arange(P, dtype=np.int64)[None, :], table, True, self.device,
-                                    stager=self.stager, extra=prompt)
+            for group in self._prefill_groups(prefill_slots):
+                prompts = [np.asarray(list(s.prompt_token_ids), dtype=np.int64) for s in group]
+                tables = [list(s.block_table) for s in group]
+                ids_cat = np.concatenate(prompts)[None, :]
+                md = build_prefill_metadata([p.size for p in prompts], tables, self.device, stager=self.stager,
+                                            extra=ids_cat)
                 h2d += self.stager.last_bytes
-                t, tl = self.model.greedy(md.extra, None, pool, table, True, step_id, metadata=md)
+                t, tl = self.model.greedy(md.extra, None, pool, tables, True, step_id, metadata=md)
                 toks.append(t)
                 tops.append(tl)
-                ids.append(slot.seq_id)
+                ids.extend(s.seq_id for s in group)
             if decode_slots:
                 tok_ids = np.asarray([[s.current_token_id] for s in decode_slots], dtype=np.int64)
                 pos = np.asarray([[s.current_len - 1] for s in decode_slots], dtype=np.int64)

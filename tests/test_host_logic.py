@@ -164,3 +164,20 @@ def test_vocab_slices_cover_the_vocabulary_once():
             assert spans[0][0] == 0 and spans[-1][1] == V
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
             assert all(e > s for s, e in spans)
+
+
+def test_prefill_layout_positions_and_sequence_bounds():
+    from pythonintern_b200.model.metadata import prefill_layout
+    pos, tidx, ctx, seq_start, last, c0 = prefill_layout([3, 1, 2])
+    assert pos.tolist() == [0, 1, 2, 0, 0, 1]  # arange(P) per prompt (execution_engine.py:88-93)
+    assert tidx.tolist() == [0, 0, 0, 1, 2, 2]
+    assert ctx.tolist() == [1, 2, 3, 1, 1, 2]
+    assert seq_start.tolist() == [0, 3, 4, 6] and seq_start.dtype == np.int32
+    assert last.tolist() == [2, 3, 5] and c0 is None
+    pos, _, ctx, _, _, c0 = prefill_layout([2, 2], ctx0=[0, 16])
+    assert pos.tolist() == [0, 1, 16, 17] and ctx.tolist() == [1, 2, 17, 18] and c0.tolist() == [0, 16]
+    for bad in ([], [2, 0], [-1]):
+        with pytest.raises(ValueError):
+            prefill_layout(bad)
+    with pytest.raises(ValueError):
+        prefill_layout([2], ctx0=[-1])
