@@ -260,14 +260,17 @@ __device__ __forceinline__ void unpack8(const uint4& raw, float (&o)[8], bool bf
 }
 
 // Second half of the fused row-parallel all-reduce (flag free).  Slot b = epoch % 3.
-//  A. CTA c < R owns row rank*R + c: it waits for each source's partial row in its receive
+//  A. CTA c owns rows rank*R + c, + gridDim.x, ... (a prefill can give a rank more rows
+//     than the grid has CTAs): per row it waits for each source's partial in its receive
 //     slot b, sums them in rank order, adds the float32 residual slice, normalises, and
-//     stores the normalised row into slot b of EVERY rank's all-gather buffer.
+//     stores the normalised row into slot b of EVERY rank's all-gather buffer.  Part A
+//     waits only on the peers' GEMMs, never on another CTA of this grid, and every CTA
+//     finishes its part A rows before part C, so the grid-stride loop cannot deadlock.
 //  B. every CTA refills its share of the slots used by the previous call ((b + 2) % 3)
 //     with the sentinel.
 //  C. every CTA waits for its share of rows of its own all-gather slot b and copies them
 //     to y (the caller's [rows, dim] output).
-template <typename T>
+template <typename T, bool MULTI>
 __global__ void __launch_bounds__(512) allreduce_rmsnorm_sharded_kernel(CommView v, int rows, int R, int dim, float* h_slice,
                                                  const float* __restrict__ w, float eps, T* __restrict__ y,
                                                  int64_t timeout_ns, int32_t* status) {
@@ -292,9 +295,8 @@ __global__ void __launch_bounds__(512) allreduce_rmsnorm_sharded_kernel(CommView
   }
   __syncthreads();
 
-  // A. reduce the owned row
-  const int row = v.rank * R + blockIdx.x;
-  if (blockIdx.x < R && row < rows) {
+  // A. reduce the owned rows (MULTI: more owned rows than CTAs, each CTA loops)
+  auto reduce_row = [&](const int rr, const int row) {
     const T* recv = reinterpret_cast<const T*>(v.recv_own[b]);
     float hv[4][8];
     float4 wv[4][2];
@@ -304,7 +306,7 @@ __global__ void __launch_bounds__(512) allreduce_rmsnorm_sharded_kernel(CommView
       const int j = threadIdx.x + it * blockDim.x;
       if (j >= nv) continue;
       // residual and norm weight are requested first; they do not depend on the partials
-      float* hp = h_slice + (size_t)blockIdx.x * dim + j * 8;
+      float* hp = h_slice + (size_t)rr * dim + j * 8;
       const float4 h0 = *reinterpret_cast<const float4*>(hp);
       const float4 h1 = *reinterpret_cast<const float4*>(hp + 4);
       wv[it][0] = __ldg(reinterpret_cast<const float4*>(w + j * 8));
@@ -317,14 +319,14 @@ __global__ void __launch_bounds__(512) allreduce_rmsnorm_sharded_kernel(CommView
 #pragma unroll
       for (int src = 0; src < kMaxRanks; ++src) {
         if (src >= v.world) break;
-        const T* ptr = recv + ((size_t)src * R + blockIdx.x) * dim + j * 8;
+        const T* ptr = recv + ((size_t)src * R + rr) * dim + j * 8;
 #pragma unroll
         for (int h = 0; h < NV16; ++h) raw[src * NV16 + h] = ld_volatile16(ptr + h * (8 / NV16));
       }
 #pragma unroll
       for (int src = 0; src < kMaxRanks; ++src) {
         if (src >= v.world) break;
-        const T* ptr = recv + ((size_t)src * R + blockIdx.x) * dim + j * 8;
+        const T* ptr = recv + ((size_t)src * R + rr) * dim + j * 8;
 #pragma unroll
         for (int h = 0; h < NV16; ++h)
           if (has_sentinel<T>(raw[src * NV16 + h])) raw[src * NV16 + h] = wait16<T>(ptr + h * (8 / NV16), deadline, &ok);
@@ -362,6 +364,16 @@ __global__ void __launch_bounds__(512) allreduce_rmsnorm_sharded_kernel(CommView
       for (int q = 0; q < v.world; ++q)
         store8<T>(reinterpret_cast<T*>(v.xn[b][q]) + (size_t)row * dim + j * 8, o);
     }
+  };
+  if constexpr (MULTI) {
+    for (int rr = blockIdx.x; rr < R; rr += gridDim.x) {
+      const int row = v.rank * R + rr;
+      if (row >= rows) break;
+      reduce_row(rr, row);
+    }
+  } else {
+    const int row = v.rank * R + blockIdx.x;
+    if (blockIdx.x < R && row < rows) reduce_row(blockIdx.x, row);
   }
 
   // B. re-arm the previous call's slots (receive slot and own all-gather slot) over the
@@ -769,16 +781,20 @@ int b2_allreduce_rmsnorm_sharded(b2_comm* comm, int rows, int dim, int dtype, fl
                "b2_allreduce_rmsnorm_sharded: h_slice, norm_w and y must be 16-byte aligned");
   const b2::CommView v = b2::make_view(comm);
   int grid = R < 64 ? 64 : R;
-  if (grid > b2::kMaxCtas) grid = b2::kMaxCtas;
-  B2_CHECK_ARG(R <= grid, "b2_allreduce_rmsnorm_sharded: %d rows per rank exceed %d", R, b2::kMaxCtas);
+  if (grid > b2::kMaxCtas) grid = b2::kMaxCtas;  // more rows per rank: each CTA loops over several
   int threads = 64;  // one 8-element vector per thread per row up to dim 4096
   while (threads < 512 && threads < dim / 8) threads *= 2;
+  const bool multi = R > grid;
   if (dtype == B2_BF16)
-    B2_TRY_CUDA(b2::launch_pdl((b2::allreduce_rmsnorm_sharded_kernel<__nv_bfloat16>), dim3(grid), dim3(threads), 0,
-                               stream, v, rows, R, dim, h_slice, norm_w, eps, (__nv_bfloat16*)y, timeout_ns, status));
+    B2_TRY_CUDA(b2::launch_pdl(multi ? b2::allreduce_rmsnorm_sharded_kernel<__nv_bfloat16, true>
+                                     : b2::allreduce_rmsnorm_sharded_kernel<__nv_bfloat16, false>,
+                               dim3(grid), dim3(threads), 0, stream, v, rows, R, dim, h_slice, norm_w, eps,
+                               (__nv_bfloat16*)y, timeout_ns, status));
   else
-    B2_TRY_CUDA(b2::launch_pdl((b2::allreduce_rmsnorm_sharded_kernel<float>), dim3(grid), dim3(threads), 0,
-                               stream, v, rows, R, dim, h_slice, norm_w, eps, (float*)y, timeout_ns, status));
+    B2_TRY_CUDA(b2::launch_pdl(multi ? b2::allreduce_rmsnorm_sharded_kernel<float, true>
+                                     : b2::allreduce_rmsnorm_sharded_kernel<float, false>,
+                               dim3(grid), dim3(threads), 0, stream, v, rows, R, dim, h_slice, norm_w, eps, (float*)y,
+                               timeout_ns, status));
   B2_TRY_CUDA(cudaGetLastError());
   return B2_OK;
 }

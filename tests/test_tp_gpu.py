@@ -72,6 +72,53 @@ def test_row_parallel_linear_with_in_memory_comm():
         c.cleanup()
 
 
+@pytest.mark.skipif(NGPU < 2, reason="needs 2 GPUs")
+def test_sharded_allreduce_rmsnorm_more_rows_than_ctas():
+    """A prefill-sized call: 600 rows give each of 2 ranks 300 rows, more than the kernel's
+    128 CTAs, so every CTA reduces several rows.  Against torch float32 on the same inputs."""
+    from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
+    from pythonintern_b200.tensor_parallel.layers import RowParallelLinear
+    T, K, H, eps = 600, 256, 512, 1e-5
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn(T, K, generator=gen).to(torch.bfloat16)
+    w = (torch.randn(K, H, generator=gen) * 0.05).to(torch.bfloat16)
+    resid = torch.randn(T, H, generator=gen)
+    nw = torch.rand(H, generator=gen) + 0.5
+    hs = resid + x.float() @ w.float()
+    want = hs * torch.rsqrt(hs.pow(2).mean(-1, keepdim=True) + eps) * nw
+    comms = [DistributedCommunicator(rank=r, world_size=2, device=f"cuda:{r}") for r in range(2)]
+    comms[0].register_in_memory_peer(1, comms[1])
+    comms[1].register_in_memory_peer(0, comms[0])
+    out = [None, None]
+    hout = [None, None]
+
+    def run(r):
+        dev = f"cuda:{r}"
+        with torch.cuda.device(r):
+            m = RowParallelLinear(K, H, bias=False, rank=r, world_size=2, communicator=comms[r],
+                                  dtype=torch.bfloat16, device=dev)
+            with torch.no_grad():
+                m.weight.copy_(w[r * K // 2:(r + 1) * K // 2])
+            r0, r1, R = comms[r].row_slice(T)
+            h = torch.zeros(R, H, device=dev)
+            h[: r1 - r0] = resid[r0:r1].to(dev)
+            comms[r].row_parallel_linear(x[:, r * K // 2:(r + 1) * K // 2].contiguous().to(dev), m.packed_weight())
+            y = comms[r].allreduce_rmsnorm_sharded(T, H, torch.bfloat16, h, nw.to(dev), eps)
+            torch.cuda.synchronize()
+            out[r] = y.float().cpu()
+            hout[r] = h[: r1 - r0].cpu()
+    th = [threading.Thread(target=run, args=(r,)) for r in range(2)]
+    [t.start() for t in th]
+    [t.join() for t in th]
+    for r in range(2):
+        assert float((out[r] - want).norm() / want.norm()) < 2e-2
+    assert torch.equal(out[0], out[1])  # every rank gets the same all-gathered rows
+    got_h = torch.cat(hout)
+    assert float((got_h - hs).norm() / hs.norm()) < 1e-2
+    for c in comms:
+        c.cleanup()
+
+
 @pytest.mark.skipif(NGPU < 4, reason="needs 4 GPUs")
 def test_all_reduce_4_ranks():
     from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
