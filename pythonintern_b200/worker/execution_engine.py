@@ -34,6 +34,26 @@ from pythonintern_b200.worker.graphs import DecodeGraphCache
 from pythonintern_b200.worker.messages import SampledToken, StepResponse
 
 
+def group_prefills(prompt_lens: List[int], max_tokens: int, batch: bool = True) -> List[List[int]]:
+    """Indices of consecutive prefill slots packed into groups of at most ``max_tokens``
+    prompt tokens (a longer prompt forms a group of its own); ``batch=False`` gives one
+    group per prompt, the reference's loop (execution_engine.py:85-111)."""
+    if not batch:
+        return [[i] for i in range(len(prompt_lens))]
+    groups: List[List[int]] = []
+    cur: List[int] = []
+    n = 0
+    for i, P in enumerate(prompt_lens):
+        if cur and n + P > max_tokens:
+            groups.append(cur)
+            cur, n = [], 0
+        cur.append(i)
+        n += P
+    if cur:
+        groups.append(cur)
+    return groups
+
+
 class WorkerExecutionEngine:
     def __init__(self, model_config: ModelConfig, shard_config: ShardConfig, kv_config: KVCacheConfig,
                  communicator: Optional[DistributedCommunicator] = None, device="cuda",
@@ -97,21 +117,9 @@ class WorkerExecutionEngine:
         return self._pin_tok[:n].numpy(), self._pin_top[:n].numpy()
 
     def _prefill_groups(self, slots) -> List[list]:
-        """Consecutive prefill slots packed into groups of at most ``max_prefill_tokens``
-        prompt tokens (a longer prompt forms a group of its own)."""
-        if not self.batch_prefills:
-            return [[s] for s in slots]
-        groups, cur, n = [], [], 0
-        for s in slots:
-            P = len(s.prompt_token_ids)
-            if cur and n + P > self.max_prefill_tokens:
-                groups.append(cur)
-                cur, n = [], 0
-            cur.append(s)
-            n += P
-        if cur:
-            groups.append(cur)
-        return groups
+        """The step's prefill slots in groups of at most ``max_prefill_tokens`` prompt tokens."""
+        idx = group_prefills([len(s.prompt_token_ids) for s in slots], self.max_prefill_tokens, self.batch_prefills)
+        return [[slots[i] for i in g] for g in idx]
 
     def execute_step(self, step_request) -> StepResponse:
         start = time.perf_counter()

@@ -181,3 +181,11 @@ def test_prefill_layout_positions_and_sequence_bounds():
             prefill_layout(bad)
     with pytest.raises(ValueError):
         prefill_layout([2], ctx0=[-1])
+
+
+def test_group_prefills_respects_the_token_cap():
+    from pythonintern_b200.worker.execution_engine import group_prefills
+    assert group_prefills([60, 30, 20, 150, 5], 100) == [[0, 1], [2], [3], [4]]
+    assert group_prefills([10, 10, 10], 100) == [[0, 1, 2]]
+    assert group_prefills([10, 10, 10], 100, batch=False) == [[0], [1], [2]]
+    assert group_prefills([], 100) == []
