@@ -11,6 +11,7 @@ and the KV cache is random (synthetic data; there is no checkpoint or dataset).
   python bench.py --gpus N --steps K --warmup W           # this framework
   python bench.py --impl reference --steps K --warmup W   # reference CPU algorithm
   python bench.py --workload prefill                      # batched varlen prefill (below)
+  torchrun --nproc-per-node N bench.py --workload allreduce   # row-parallel all-reduce (below)
 
 One JSON line on rank 0:
   value        decode tokens/s with inputs resident in HBM (CUDA events, max over ranks)
@@ -26,6 +27,13 @@ One JSON line on rank 0:
 Mistral-7B shape (vocab 32000), 16 prompts of 1024 tokens prefilled in ONE batched
 forward (the reference runs one forward per prompt), metric prefill tokens/s; the
 roofline is the dominant kernel's TFLOP/s against the bf16 tensor peak.
+
+``--workload allreduce`` (N >= 2 ranks) is the row-parallel microbenchmark: bf16
+X [T, 14336/N] x W [14336/N, 4096], then all-reduce(SUM) + float32 residual + RMSNorm,
+for T in 1, 8, 64, 512, 4096, as ONE fused pair of launches (the GEMM epilogue pushes
+partial rows to their owners over NVLink; the owners reduce, normalise and all-gather).
+Metric: bus GB/s = 2 (N - 1) / N * T * 4096 * 2 B / time at T = 4096, beside an NCCL
+all-reduce of the same payload and the GEMM alone.
 """
 
 from __future__ import annotations
@@ -70,7 +78,7 @@ def parse_args(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-batch", type=int, default=4)
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "allreduce"], default="decode")
     ap.add_argument("--prompts", type=int, default=16, help="prefill workload: prompts per step")
     ap.add_argument("--prompt-len", type=int, default=1024, help="prefill workload: tokens per prompt")
     return ap.parse_args(argv)
@@ -800,12 +808,129 @@ def run_prefill(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- row-parallel all-reduce
+def run_allreduce(args):
+    import torch
+    import torch.distributed as dist
+
+    from pythonintern_b200 import _lib, kernels
+    from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world < 2:
+        print(json.dumps({"metric": "row-parallel all-reduce bus GB/s", "unavailable":
+                          "needs >= 2 ranks (torchrun --nproc-per-node N)"}), flush=True)
+        return 0
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    H, I = 4096, 14336
+    Tmax = 4096
+    K = I // world
+    comm = DistributedCommunicator(rank, world, device=dev, max_bytes=max(64 << 20, Tmax * H * 2))
+    comm.connect()
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 1 + rank)
+    w = (torch.randn(H, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)  # packed [out, in] rows
+    nw = torch.ones(H, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def max_over_ranks(x: float) -> float:
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def time_graph(fn, n, reps=5):
+        """Device seconds per call: n calls captured in one graph, replayed `reps` times, max over ranks."""
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for _ in range(n):
+                fn()
+        dist.barrier()
+        gr.replay()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            gr.replay()
+        e1.record(stream)
+        e1.synchronize()
+        del gr
+        return max_over_ranks(e0.elapsed_time(e1) / (reps * n) / 1000.0)
+
+    rows = []
+    clocks = ClockSampler(local)
+    clocks.start()
+    for T in (1, 8, 64, 512, 4096):
+        x = torch.randn(T, K, device=dev, generator=g).to(torch.bfloat16)
+        r0, r1, R = comm.row_slice(T)
+        h = torch.zeros(R, H, device=dev)
+        y = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
+        n = 20 if T <= 512 else 6  # an even count keeps the exchange slots in step
+
+        def fused():
+            comm.row_parallel_linear(x, w)
+            comm.allreduce_rmsnorm_sharded(T, H, torch.bfloat16, h, nw, 1e-5, out=y)
+        t_fused = time_graph(fused, n)
+        t_gemm = time_graph(lambda: kernels.linear(x, w), n)
+        payload = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+        for _ in range(3):
+            dist.all_reduce(payload)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            dist.all_reduce(payload)
+        e1.record(stream)
+        e1.synchronize()
+        t_nccl = max_over_ranks(e0.elapsed_time(e1) / n / 1000.0)
+        nbytes = T * H * 2
+        bus = 2 * (world - 1) / world * nbytes
+        rows.append({"tokens": T, "payload_bytes": nbytes, "fused_us": t_fused * 1e6, "gemm_alone_us": t_gemm * 1e6,
+                     "fused_bus_gbs": bus / t_fused / 1e9, "nccl_allreduce_us": t_nccl * 1e6,
+                     "nccl_bus_gbs": bus / t_nccl / 1e9,
+                     "gemm_plus_nccl_us": (t_gemm + t_nccl) * 1e6})
+    clk = clocks.stop()
+    _lib.check_device_status(dev, "all-reduce microbenchmark")
+    if rank == 0:
+        top = rows[-1]
+        line = {
+            "metric": "row-parallel all-reduce bus GB/s", "value": top["fused_bus_gbs"], "unit": "GB/s",
+            "n_gpus": world, "steps": None, "warmup": 2, "ms_per_step": top["fused_us"] / 1000.0,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded N(0,1) activations, N(0,0.02) weights",
+            "config": {"workload": (f"row-parallel GEMM [T, {I}/{world}] x [{I}/{world}, {H}] + all-reduce + residual "
+                                    f"+ RMSNorm, TP={world}; value at T=4096"),
+                       "parallelism": f"tp{world}", "tokens": [r["tokens"] for r in rows]},
+            "nvlink_peak_gbs_per_direction": 770.0,
+            "note": ("fused_us includes the GEMM (its epilogue pushes the partial rows); bus GB/s counts the "
+                     "all-reduce payload only, so the GEMM's time lowers it; gemm_plus_nccl_us is the unfused "
+                     "alternative (GEMM, then an NCCL all-reduce, without the residual and RMSNorm)"),
+            "clocks": clk, "sizes": rows,
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    comm.cleanup()
+    dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "prefill":
         return run_prefill(args)
+    if args.workload == "allreduce":
+        return run_allreduce(args)
     return run_ours(args)
 
 
