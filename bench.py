@@ -429,9 +429,6 @@ def run_ours(args):
         "gate_up_swiglu": (lambda r=0: kernels.linear_swiglu(xn, lay[r % L].mlp.gate_proj.packed_weight(),
                                                              lay[r % L].mlp.up_proj.packed_weight()),
                            wbytes(ml.gate_proj.weight) + wbytes(ml.up_proj.weight)),
-        "down": (lambda r=0: kernels.linear(torch.empty(B, ml.down_proj.in_features_per_partition, device=dev,
-                                                        dtype=model.dtype).normal_(),
-                                            lay[r % L].mlp.down_proj.packed_weight()), wbytes(ml.down_proj.weight)),
     }
     down_in = torch.randn(B, ml.down_proj.in_features_per_partition, device=dev).to(model.dtype)
     gemms["down"] = (lambda r=0: kernels.linear(down_in, lay[r % L].mlp.down_proj.packed_weight()),
@@ -461,12 +458,9 @@ def run_ours(args):
     fused_ar = None
     if world > 1:
         H = cfg.hidden_dim
-        res = torch.zeros(B, H, device=dev)
-        y = torch.empty(B, H, device=dev, dtype=model.dtype)
         nw = lay[0].post_attention_layernorm.weight
-
-        r0, r1, R = comm.row_slice(B)
-        res = torch.zeros(R, H, device=dev)
+        _, _, R = comm.row_slice(B)
+        res = torch.zeros(R, H, device=dev)  # this rank's residual rows
 
         y_ar = torch.empty(B, H, device=dev, dtype=model.dtype)
         a_in = torch.randn(B, lay[0].self_attn.out_proj.in_features_per_partition, device=dev).to(model.dtype)
