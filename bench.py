@@ -251,9 +251,41 @@ def cpu_baseline_entry(args, cfg):
                        f"extrapolated to a full decode step; TP=1 on the host cores")}
 
 
+def run_reference_prefill(args):
+    """Reference arm of the prefill workload: the oracle's one-prompt-per-forward prefill."""
+    from pythonintern_b200 import workloads
+    cfg = workloads.mistral_7b_config(num_layers=32)
+    n, P = args.prompts, args.prompt_len
+    for _ in range(max(0, args.warmup)):
+        cpu_prefill_sample(cfg, P, args.seed)
+    times = [cpu_prefill_sample(cfg, P, args.seed) * cfg.num_layers * n for _ in range(max(1, args.steps))]
+    t = statistics.median(times)
+    value = n * P / t
+    sample = (f"per step: one prompt of {P} tokens through 1 of {cfg.num_layers} decoder layers, extrapolated to "
+              f"{n} prompts x {cfg.num_layers} layers; median of {len(times)} steps")
+    line = {
+        "impl": "reference", "metric": "prefill tokens/s", "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1000.0,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"mistral-7b-shape batched prefill, {n} prompts x {P} tokens, TP=1 (CPU)",
+                   "model": "mistral-7b-shape", "global_batch": n, "seq_len": P, "parallelism": "tp1 (CPU)"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return 0
+    if args.workload == "prefill":
+        return run_reference_prefill(args)
+    if args.workload == "allreduce":
+        print(json.dumps({"impl": "reference", "metric": "row-parallel all-reduce bus GB/s",
+                          "unavailable": "the reference all-reduce runs over gRPC between worker processes; "
+                                         "it has no device path to time on these GPUs"}), flush=True)
         return 0
     cfg = model_config(32)
     b = max(1, min(args.cpu_sample_batch, args.batch))

@@ -45,3 +45,15 @@ def test_cpu_prefill_sample_and_flop_count():
     params = H * (nq + 2 * nkv) * hd + nq * hd * H + 3 * H * inter
     assert gemm == 2.0 * 5 * params * 2
     assert attn == 4.0 * (6 + 3) * hd * nq * 2  # keys: 1+2+3 and 1+2
+
+
+def test_reference_arm_prefill_workload_prints_one_json_line():
+    env = dict(os.environ, RANK="0")
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload",
+                          "prefill", "--steps", "1", "--warmup", "0", "--prompts", "2", "--prompt-len", "64"],
+                         capture_output=True, text=True, timeout=600, env=env)
+    assert out.returncode == 0, out.stderr
+    lines = [l for l in out.stdout.splitlines() if l.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["metric"] == "prefill tokens/s" and d["value"] > 0
