@@ -77,7 +77,8 @@ def parse_args(argv=None):
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-sample-batch", type=int, default=4)
+    ap.add_argument("--no-parity", action="store_true", help="skip the TP parity leg (it runs before timing)")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the row-parallel sweep at TP > 1")
     ap.add_argument("--workload", choices=["decode", "prefill", "allreduce"], default="decode")
     ap.add_argument("--prompts", type=int, default=16, help="prefill workload: prompts per step")
     ap.add_argument("--prompt-len", type=int, default=1024, help="prefill workload: tokens per prompt")
@@ -134,28 +135,73 @@ def workload_name(args, n):
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled every 200 ms during the timed region."""
+    """SM clocks and throttle reasons sampled every 10 ms (NVML, in a thread) during the timed region.
+
+    Falls back to ``nvidia-smi -lms 50`` when NVML cannot be loaded.  A short timed region
+    (a few tens of milliseconds at TP=8) still gets several samples this way.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvml.h): sw power cap 0x4, hw slowdown 0x8,
+    # sw thermal 0x20, hw thermal 0x40.
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, period_s: float = 0.01):
         self.gpu = gpu_index
+        self.period = period_s
         self.proc = None
         self.path = None
+        self.thread = None
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self.stop_flag = None
 
     def start(self):
+        import threading
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+            self.stop_flag = threading.Event()
+
+            def loop():
+                while not self.stop_flag.is_set():
+                    try:
+                        self.samples.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                        bits = int(reasons_fn(h))
+                        for nm, b in self.BITS.items():
+                            if bits & b:
+                                self.reasons.add(nm)
+                    except Exception:
+                        pass
+                    self.stop_flag.wait(self.period)
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         fd, self.path = tempfile.mkstemp(prefix="b2clk", suffix=".csv")
         os.close(fd)
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.gpu)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=2)
+            sm = self.samples
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                    "reasons": sorted(self.reasons), "samples": len(sm), "source": "NVML, 10 ms period"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
         self.proc.terminate()
@@ -180,61 +226,10 @@ class ClockSampler:
                         reasons.add(nm)
         os.unlink(self.path)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi, 50 ms period"}
 
 
 # ----------------------------------------------------------------------------- CPU leg
-def cpu_sample(cfg, batch: int, ctx: int, seed: int, reps: int = 1):
-    """Oracle (numpy float32) timing of one decoder layer + an lm_head slice; returns step seconds.
-
-    The sample decodes ``batch`` sequences at context ``ctx`` through one decoder layer
-    of the configured shape (the reference's per-sequence gather, zero padding,
-    repeat_kv and float32 arithmetic, restated in oracle/), and multiplies the
-    final hidden states by a 1/8 slice of the lm_head; the step time is
-    layer_time * num_layers + slice_time * 8.
-    """
-    import oracle
-    from oracle import decoder as od
-    od.set_precision(np.float32)
-    rng = np.random.default_rng(seed)
-    H, hd, nq, nkv, inter = cfg.hidden_dim, cfg.head_dim, cfg.num_heads, cfg.num_kv_heads, cfg.intermediate_dim
-    ocfg = oracle.OracleConfig(cfg.vocab_size, H, 1, nq, nkv, inter, max(cfg.max_seq_len, ctx + 8), cfg.rms_norm_eps)
-    std = np.float32(0.02)
-    shard = {
-        "layers.0.input_layernorm.weight": np.ones(H, np.float32),
-        "layers.0.post_attention_layernorm.weight": np.ones(H, np.float32),
-        "layers.0.self_attn.q_proj.weight": rng.standard_normal((H, nq * hd), np.float32) * std,
-        "layers.0.self_attn.k_proj.weight": rng.standard_normal((H, nkv * hd), np.float32) * std,
-        "layers.0.self_attn.v_proj.weight": rng.standard_normal((H, nkv * hd), np.float32) * std,
-        "layers.0.self_attn.out_proj.weight": rng.standard_normal((nq * hd, H), np.float32) * std,
-        "layers.0.mlp.gate_proj.weight": rng.standard_normal((H, inter), np.float32) * std,
-        "layers.0.mlp.up_proj.weight": rng.standard_normal((H, inter), np.float32) * std,
-        "layers.0.mlp.down_proj.weight": rng.standard_normal((inter, H), np.float32) * std,
-    }
-    bps = math.ceil((ctx + 1) / 16)
-    pool = oracle.KVPool(1, batch * bps, 16, nkv, hd)
-    pool.k[:] = rng.standard_normal(pool.k.shape, np.float32)
-    pool.v[:] = rng.standard_normal(pool.v.shape, np.float32)
-    perm = rng.permutation(batch * bps)
-    tables = [list(perm[b * bps:(b + 1) * bps]) for b in range(batch)]
-    model = oracle.OracleModel(ocfg, [shard], [pool], cos=None, sin=None)
-    h = rng.standard_normal((batch, 1, H), np.float32)
-    pos = np.full((batch, 1), ctx - 1, dtype=np.int64)
-    vs = cfg.vocab_size // 8
-    lm = rng.standard_normal((vs, H), np.float32) * std
-    best = None
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        y = model.block(0, h, pos, tables, False)
-        t1 = time.perf_counter()
-        od.rmsnorm(y[:, -1], np.ones(H, np.float32), 1e-5) @ lm.T
-        t2 = time.perf_counter()
-        step = (t1 - t0) * cfg.num_layers + (t2 - t1) * (cfg.vocab_size / vs)
-        best = step if best is None else min(best, step)
-    od.set_precision(np.float64)
-    return best
-
-
 def cpu_cores():
     try:
         return len(os.sched_getaffinity(0))
@@ -242,13 +237,38 @@ def cpu_cores():
         return os.cpu_count() or 1
 
 
+def cpu_decode(cfg, world: int, batch: int, ctx: int, steps: int, warmup: int, seed: int, cores: int):
+    """The reference's CPU decode, restated on torch CPU (oracle/grpc_tp.py), timed on this host.
+
+    ``world`` rank processes (``cores // world`` threads each) each run their shard of ONE
+    decoder layer of ``cfg``'s shape for ``batch`` sequences at context ``ctx`` (paged pool,
+    permuted block tables, zero padding, repeat_kv, float32), joined by the reference's
+    gRPC all-reduce after out_proj and down_proj, plus 1/8 of the replicated lm_head.
+    Returns the oracle timing dict: per-step seconds extrapolated to all layers and the
+    whole lm_head (max over ranks), the sampled wall times and the thread counts.
+    """
+    from oracle import grpc_tp
+    return grpc_tp.time_tp_decode(world, cfg.hidden_dim, cfg.num_heads, cfg.num_kv_heads, cfg.intermediate_dim,
+                                  cfg.vocab_size, cfg.num_layers, batch, ctx, steps, warmup, seed, cores)
+
+
+def cpu_sample_text(cfg, world, batch, ctx, r):
+    ex = (f"; the {world} rank processes exchange partial sums over the reference's gRPC all-reduce "
+          f"(protobuf AllReducePayload on localhost)") if world > 1 else ""
+    return (f"torch-CPU restatement of the reference's float32 decode path: {batch} sequences at context {ctx}, "
+            f"1 of {cfg.num_layers} decoder layers + 1/{round(cfg.vocab_size / r['vocab_slice'])} of the lm_head "
+            f"timed per step and extrapolated to the full step; TP={world}, {r['threads_per_rank']} threads per "
+            f"rank{ex}")
+
+
 def cpu_baseline_entry(args, cfg):
-    b = max(1, min(args.cpu_sample_batch, args.batch))
-    t = cpu_sample(cfg, b, args.ctx, args.seed)
-    return {"value": b / t, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
-            "sample": (f"oracle (numpy float32 restatement of the reference CPU path) on {b} sequences at "
-                       f"context {args.ctx}: 1 of {cfg.num_layers} decoder layers + 1/8 of the lm_head, "
-                       f"extrapolated to a full decode step; TP=1 on the host cores")}
+    """Bounded sample for the GPU arm's line (rank 0 at N=1): one warm-up and one timed step."""
+    cores = cpu_cores()
+    r = cpu_decode(cfg, 1, args.batch, args.ctx, 1, 1, args.seed, cores)
+    t = statistics.median(r["step_s"])
+    return {"value": args.batch / t, "unit": "tokens/s", "cores": sum(r["threads_used"]), "kind": "port",
+            "sample": cpu_sample_text(cfg, 1, args.batch, args.ctx, r), "batch": args.batch, "layers_sampled": 1,
+            "sample_s": r["sample_wall_s"][0]}
 
 
 def run_reference_prefill(args):
@@ -277,36 +297,341 @@ def run_reference_prefill(args):
 
 
 def run_reference(args):
+    """Reference arm: the reference's CPU path (restated, oracle/grpc_tp.py) on this host's cores.
+
+    Under torchrun only rank 0 works; it starts ``world`` CPU rank processes itself (the
+    reference runs one worker process per shard) and splits the host's cores among them.
+    """
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return 0
     if args.workload == "prefill":
         return run_reference_prefill(args)
     if args.workload == "allreduce":
-        print(json.dumps({"impl": "reference", "metric": "row-parallel all-reduce bus GB/s",
-                          "unavailable": "the reference all-reduce runs over gRPC between worker processes; "
-                                         "it has no device path to time on these GPUs"}), flush=True)
-        return 0
+        return run_reference_allreduce(args, world)
     cfg = model_config(32)
-    b = max(1, min(args.cpu_sample_batch, args.batch))
-    for _ in range(max(0, args.warmup)):
-        cpu_sample(cfg, b, args.ctx, args.seed)
-    times = [cpu_sample(cfg, b, args.ctx, args.seed) for _ in range(max(1, args.steps))]
-    t = statistics.median(times)
-    value = b / t
+    cores = cpu_cores()
+    r = cpu_decode(cfg, world, args.batch, args.ctx, max(1, args.steps), max(0, args.warmup), args.seed, cores)
+    t = statistics.median(r["step_s"])
+    value = args.batch / t
     line = {
         "impl": "reference", "metric": "decode tokens/s", "value": value, "unit": "tokens/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1000.0,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1000.0,
+        "sample_ms_per_step": statistics.median(r["sample_wall_s"]) * 1000.0,
+        "ms_per_step_note": ("ms_per_step is the full 32-layer step extrapolated from the timed sample "
+                             "(1 decoder layer + 1/8 of the lm_head per step); sample_ms_per_step is the wall "
+                             "time each timed step actually took"),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": workload_name(args, 1), "model": "llama3-8b-shape",
-                                        "global_batch": args.batch, "seq_len": args.ctx, "parallelism": "tp1 (CPU)"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
-                         "sample": f"per step: 1 of 32 decoder layers + 1/8 lm_head on {b} sequences at "
-                                   f"context {args.ctx}, extrapolated; median of {len(times)} steps"},
+        "data": "synthetic: N(0,0.02) weights, random KV cache, random block-table permutation",
+        "config": decode_config(args, world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": sum(r["threads_used"]), "kind": "port",
+                         "sample": cpu_sample_text(cfg, world, args.batch, args.ctx, r) +
+                         f"; median of {len(r['step_s'])} steps",
+                         "batch": args.batch, "layers_sampled": 1, "threads_per_rank": r["threads_per_rank"],
+                         "ranks": world, "host_cores": cores},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+ROWPAR_TOKENS = (1, 8, 64, 512, 4096)
+
+
+def run_reference_allreduce(args, world):
+    """Reference arm of the row-parallel microbenchmark: float32 partial GEMM + gRPC all-reduce +
+    residual + RMSNorm across ``world`` CPU rank processes (the reference has no bf16 path)."""
+    if world < 2:
+        print(json.dumps({"impl": "reference", "metric": "row-parallel all-reduce bus GB/s",
+                          "unavailable": "needs >= 2 ranks (torchrun --nproc-per-node N)"}), flush=True)
+        return 0
+    from oracle import grpc_tp
+    H, I = 4096, 14336
+    cores = cpu_cores()
+    r = grpc_tp.time_row_parallel(world, ROWPAR_TOKENS, H, I, args.seed, cores)
+    rows = []
+    for T, t in zip(ROWPAR_TOKENS, r["s"]):
+        nbytes = T * H * 4
+        rows.append({"tokens": T, "payload_bytes": nbytes, "us": t * 1e6,
+                     "bus_gbs": 2 * (world - 1) / world * nbytes / t / 1e9})
+    top = rows[-1]
+    line = {
+        "impl": "reference", "metric": "row-parallel all-reduce bus GB/s", "value": top["bus_gbs"], "unit": "GB/s",
+        "n_gpus": world, "steps": None, "warmup": 1, "ms_per_step": top["us"] / 1000.0,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded activations, N(0,0.02) weights",
+        "config": rowpar_config(world),
+        "cpu_baseline": {"value": top["bus_gbs"], "unit": "GB/s", "cores": sum(r["threads_used"]), "kind": "port",
+                         "sample": (f"torch-CPU restatement of RowParallelLinear.forward + the reference's gRPC "
+                                    f"all-reduce across {world} rank processes ({r['threads_per_rank']} threads each) "
+                                    f"+ residual + RMSNorm, float32 payload (the reference has no bf16 path); best "
+                                    f"of 3 calls (1 at 4096 tokens) after one warm-up")},
+        "e2e": {"value": top["bus_gbs"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "sizes": rows,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def decode_config(args, world):
+    return {"workload": workload_name(args, world), "model": "llama3-8b-shape", "global_batch": args.batch,
+            "seq_len": args.ctx, "parallelism": f"tp{world}",
+            "l2": "inputs larger than L2 (weights + KV read per step >> 126 MB)"}
+
+
+def rowpar_config(world):
+    return {"workload": (f"row-parallel GEMM [T, 14336/{world}] x [14336/{world}, 4096] + all-reduce + residual "
+                         f"+ RMSNorm, TP={world}; value at T=4096"),
+            "parallelism": f"tp{world}", "tokens": list(ROWPAR_TOKENS)}
+
+
+# ----------------------------------------------------------------------------- parity leg
+PARITY_FIXTURE = os.path.join(ROOT, "tests", "golden", "llama3_8b_layer_parity.npz")
+PARITY_TOL = 2e-2  # bf16: relative Frobenius error of the residual stream after the layer
+
+
+def tp_parity(comm, rank: int, world: int, dev) -> dict:
+    """Checks the CUDA path at TP=world against committed fixtures before anything is timed.
+
+    * One Llama-3-8B-shape decoder layer (vocabulary 4096, seeded N(0, 0.02) weights
+      sharded by WeightSharder): two prompts of 40 and 13 tokens prefilled in one varlen
+      call, then two batched decode steps fed the fixture's tokens.  The residual stream
+      after the layer, gathered over the ranks' row slices, must be within relative 2e-2
+      of the oracle's (tests/golden/llama3_8b_layer_parity.npz, made by
+      tests/golden/make_tp_parity.py); the greedy tokens (vocab-parallel exchange at
+      TP>1) must equal the oracle's wherever its top-2 margin exceeds the measured logit
+      error, and be identical on every rank.
+    * At TP=1 and TP=2, the float32 Tiny LLaMA workload (8 requests, 32 greedy steps
+      through execute_step) must give exactly the tokens the reference itself produced
+      (tests/golden/tiny_e2e_tp{1,2}.npz).
+    Every rank takes the same collective steps; the result is the same dict on all ranks.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from pythonintern_b200 import _lib, workloads
+    from pythonintern_b200.model.kv_cache import PhysicalKVCachePool
+    from pythonintern_b200.model.llama import DistributedLLaMAModel
+    from pythonintern_b200.model.metadata import build_metadata, build_prefill_metadata
+    from pythonintern_b200.tensor_parallel.sharding import WeightSharder
+
+    fx = np.load(PARITY_FIXTURE)
+    cfg = workloads.llama3_8b_config(num_layers=1, max_seq_len=512)
+    cfg.vocab_size = 4096
+    sd = WeightSharder(cfg, world).shard_full_model_state_dict(workloads.synthetic_state_dict(cfg, seed=21), rank)
+    model = DistributedLLaMAModel(cfg, rank, world, comm, device=dev)
+    model.load_state_dict(sd)
+    del sd
+    pool = PhysicalKVCachePool(16, 16, max(1, cfg.num_kv_heads // world), cfg.head_dim, 1, dev, "bfloat16")
+    prompts = [fx["prompt0"], fx["prompt1"]]
+    lens = [int(p.size) for p in prompts]
+    tables = [[3, 9, 1, 12], [5, 0]]
+    err2 = torch.zeros((), dtype=torch.float64, device=dev)
+    ref2 = torch.zeros((), dtype=torch.float64, device=dev)
+    logit_err = 0.0
+    toks_gpu, toks_fwd = [], []
+
+    def accumulate(tr, ref):
+        nonlocal err2, ref2
+        if world > 1:
+            r0, rows = tr
+        else:
+            r0, rows = 0, tr
+        want = torch.from_numpy(ref[r0:r0 + rows.shape[0]].astype(np.float32)).to(dev, torch.float64)
+        got = rows.reshape(rows.shape[0], -1).to(torch.float64)
+        err2 += (got - want).pow(2).sum()
+        ref2 += want.pow(2).sum()
+
+    with torch.no_grad():
+        ids = torch.from_numpy(np.concatenate(prompts)[None]).to(dev)
+        md = build_prefill_metadata(lens, tables, dev)
+        tr = []
+        logits = model(ids, None, pool, tables, True, 0, metadata=md, trace=tr)
+        accumulate(tr[0], fx["hidden_prefill"])
+        logit_err = max(logit_err, float((logits.cpu() - torch.from_numpy(fx["logits"][0])).abs().max()))
+        toks_fwd.append(logits.argmax(-1).cpu())
+        tok, _ = model.greedy(ids, None, pool, tables, True, 0, metadata=md)
+        toks_gpu.append(tok.view(-1).cpu())
+        for s in range(2):
+            feed = torch.from_numpy(fx["tokens"][s]).view(2, 1).to(dev)
+            pos = torch.tensor([[lens[0] + s], [lens[1] + s]])
+            md = build_metadata(pos, tables, False, dev)
+            tr = []
+            logits = model(feed, pos, pool, tables, False, s + 1, metadata=md, trace=tr)
+            accumulate(tr[0], fx["hidden_decode"][s])
+            logit_err = max(logit_err, float((logits.cpu() - torch.from_numpy(fx["logits"][s + 1])).abs().max()))
+            toks_fwd.append(logits.argmax(-1).cpu())
+            tok, _ = model.greedy(feed, pos, pool, tables, False, s + 1, metadata=md)
+            toks_gpu.append(tok.view(-1).cpu())
+        torch.cuda.synchronize(dev)
+        _lib.check_device_status(dev, "parity layer")
+    gpu_tok = torch.stack(toks_gpu).to(dev)
+    stats = torch.stack([err2, ref2])
+    lerr = torch.tensor([logit_err], dtype=torch.float64, device=dev)
+    tmax, tmin = gpu_tok.clone(), gpu_tok.clone()
+    if world > 1:
+        dist.all_reduce(stats)
+        dist.all_reduce(lerr, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tmin, op=dist.ReduceOp.MIN)
+    rel = float((stats[0] / stats[1]).sqrt())
+    logit_err = float(lerr.item())
+    bound = max(0.05, 3.0 * logit_err)
+    sel = fx["margins"] > bound
+    want_tok = fx["tokens"]
+    got = gpu_tok.cpu().numpy()
+    fwd = torch.stack(toks_fwd).numpy()
+    tokens_match = bool(np.array_equal(got[sel], want_tok[sel]) and np.array_equal(fwd[sel], want_tok[sel]))
+    ranks_agree = bool(torch.equal(tmax, tmin))
+    del model, pool
+    out = {"tp": world, "layer": ("llama3-8b shape, 1 layer, vocab 4096; prefill of 40 + 13 tokens, 2 decode steps; "
+                                  "oracle fixture tests/golden/llama3_8b_layer_parity.npz"),
+           "layer_rel_err": rel, "tol": PARITY_TOL, "logits_max_abs_err": logit_err,
+           "tokens_checked": int(sel.sum()), "tokens_total": int(sel.size), "token_margin_bound": bound,
+           "tokens_match": tokens_match, "ranks_agree": ranks_agree, "tiny_tokens_match": None}
+    if world <= 2:
+        out["tiny_tokens_match"] = tiny_tokens_check(comm, rank, world, dev)
+        out["tiny"] = f"Tiny LLaMA float32, 8 requests x 32 greedy steps vs the reference's own TP={world} tokens"
+    torch.cuda.empty_cache()
+    out["pass"] = bool(rel < PARITY_TOL and tokens_match and ranks_agree and out["tiny_tokens_match"] is not False)
+    return out
+
+
+def tiny_tokens_check(comm, rank: int, world: int, dev) -> bool:
+    """The Tiny LLaMA greedy workload through execute_step; True if the tokens equal the golden."""
+    import torch
+    import torch.distributed as dist
+
+    from pythonintern_b200 import workloads
+    from pythonintern_b200.config import KVCacheConfig, ShardConfig
+    from pythonintern_b200.tensor_parallel.sharding import WeightSharder
+    from pythonintern_b200.worker.execution_engine import WorkerExecutionEngine
+    from pythonintern_b200.worker.messages import SequenceSlot, StepRequest
+
+    gold = np.load(os.path.join(ROOT, "tests", "golden", f"tiny_e2e_tp{world}.npz"))
+    cfg = workloads.tiny_config()
+    eng = WorkerExecutionEngine(cfg, ShardConfig(rank, world), KVCacheConfig(16, 64, str(dev)), comm, dev)
+    full = workloads.reference_init_state_dict(cfg, 0)
+    eng.model.load_state_dict(WeightSharder(cfg, world).shard_full_model_state_dict(full, rank))
+    prompts = workloads.tiny_prompts()
+    ids = [f"req_{i}" for i in range(len(prompts))]
+    for sid, p in zip(ids, prompts):
+        eng.kv_manager.allocate_blocks_for_sequence(sid, len(p))
+    lens = {sid: len(p) for sid, p in zip(ids, prompts)}
+    cur, toks_all = {}, []
+    for step in range(gold["tokens"].shape[0]):
+        if step == 0:
+            slots = [SequenceSlot(sid, True, p, 0, len(p), list(eng.kv_manager.block_tables[sid].physical_block_ids))
+                     for sid, p in zip(ids, prompts)]
+        else:
+            slots = []
+            for sid in ids:
+                eng.kv_manager.append_token(sid)
+                lens[sid] += 1
+                slots.append(SequenceSlot(sid, False, [], cur[sid], lens[sid],
+                                          list(eng.kv_manager.block_tables[sid].physical_block_ids)))
+        resp = eng.execute_step(StepRequest(step, slots))
+        toks = [t.token_id for t in resp.sampled_tokens]
+        cur = dict(zip(ids, toks))
+        toks_all.append(toks)
+    ok = torch.tensor([1 if np.array_equal(np.asarray(toks_all), gold["tokens"]) else 0], device=dev)
+    del eng
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    return bool(ok.item())
+
+
+# ----------------------------------------------------------------------------- row-parallel sweep
+def allreduce_sweep(comm, rank: int, world: int, dev, seed: int, tokens=None) -> dict:
+    """Row-parallel GEMM [T, 14336/N] x [14336/N, 4096] + all-reduce + residual + RMSNorm per T,
+    as the fused pair of launches, beside the GEMM alone and an NCCL all-reduce of the same
+    payload (all device-timed in CUDA graphs or back-to-back launches, max over ranks), plus
+    NCCL's all-reduce bus bandwidth at 256 MB as the measured NVLink reference."""
+    import torch
+    import torch.distributed as dist
+
+    from pythonintern_b200 import _lib, kernels
+    H, I = 4096, 14336
+    K = I // world
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed + 1 + rank)
+    w = (torch.randn(H, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)  # packed [out, in] rows
+    nw = torch.ones(H, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def max_over_ranks(x: float) -> float:
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def time_graph(fn, n, reps=5):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for _ in range(n):
+                fn()
+        dist.barrier()
+        gr.replay()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            gr.replay()
+        e1.record(stream)
+        e1.synchronize()
+        del gr
+        return max_over_ranks(e0.elapsed_time(e1) / (reps * n) / 1000.0)
+
+    def time_nccl(payload, n):
+        for _ in range(3):
+            dist.all_reduce(payload)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            dist.all_reduce(payload)
+        e1.record(stream)
+        e1.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / n / 1000.0)
+
+    rows = []
+    for T in (tokens or ROWPAR_TOKENS):
+        x = torch.randn(T, K, device=dev, generator=g).to(torch.bfloat16)
+        r0, r1, R = comm.row_slice(T)
+        h = torch.zeros(R, H, device=dev)
+        y = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
+        n = 20 if T <= 512 else 6  # an even count keeps the exchange slots in step
+
+        def fused():
+            comm.row_parallel_linear(x, w)
+            comm.allreduce_rmsnorm_sharded(T, H, torch.bfloat16, h, nw, 1e-5, out=y)
+        t_fused = time_graph(fused, n)
+        t_gemm = time_graph(lambda: kernels.linear(x, w), n)
+        t_nccl = time_nccl(torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16), n)
+        nbytes = T * H * 2
+        bus = 2 * (world - 1) / world * nbytes
+        rows.append({"tokens": T, "payload_bytes": nbytes, "fused_us": t_fused * 1e6, "gemm_alone_us": t_gemm * 1e6,
+                     "fused_bus_gbs": bus / t_fused / 1e9, "nccl_allreduce_us": t_nccl * 1e6,
+                     "nccl_bus_gbs": bus / t_nccl / 1e9, "gemm_plus_nccl_us": (t_gemm + t_nccl) * 1e6,
+                     "exchange_us": (t_fused - t_gemm) * 1e6})
+        del x, h, y
+    big = torch.empty(128 << 20, dtype=torch.bfloat16, device=dev)  # 256 MB
+    t_big = time_nccl(big, 5)
+    del big
+    torch.cuda.empty_cache()
+    _lib.check_device_status(dev, "row-parallel sweep")
+    peak = 2 * (world - 1) / world * (256 << 20) / t_big / 1e9
+    return {"sizes": rows, "nvlink_peak_gbs": peak,
+            "nvlink_peak_source": f"NCCL all-reduce bus bandwidth at 256 MB, TP={world}, measured in this run",
+            "note": ("fused_us includes the GEMM (its epilogue pushes the partial rows); bus GB/s counts the "
+                     "all-reduce payload only; gemm_plus_nccl_us is the unfused alternative (GEMM, then an NCCL "
+                     "all-reduce, without the residual and RMSNorm); exchange_us = fused_us - gemm_alone_us")}
 
 
 # ----------------------------------------------------------------------------- GPU leg
@@ -336,8 +661,10 @@ def run_ours(args):
     B, ctx, W, K = args.batch, args.ctx, args.warmup, args.steps
     comm = None
     if world > 1:
-        comm = DistributedCommunicator(rank, world, device=dev, max_bytes=max(1 << 24, B * cfg.hidden_dim * 2 * 2))
+        # 64 MB holds the row-parallel sweep's largest partial (4096 tokens x 4096 bf16)
+        comm = DistributedCommunicator(rank, world, device=dev, max_bytes=max(64 << 20, B * cfg.hidden_dim * 2 * 2))
         comm.connect()
+    parity = None if args.no_parity else tp_parity(comm, rank, world, dev)
     bps = math.ceil((ctx + W + K + 2 * (W + K) + 8) / 16)
     num_blocks = B * bps
     engine = WorkerExecutionEngine(cfg, ShardConfig(rank=rank, world_size=world),
@@ -487,7 +814,7 @@ def run_ours(args):
                 "share_of_step": per_step[dominant] / 1000.0 / (ms / K)}
 
     # ---------------- fused all-reduce + residual + RMSNorm bus bandwidth (TP > 1)
-    fused_ar = None
+    fused_ar = sweep = None
     if world > 1:
         H = cfg.hidden_dim
         nw = lay[0].post_attention_layernorm.weight
@@ -526,9 +853,11 @@ def run_ours(args):
         _lib.check_device_status(dev, "all-reduce timing")
         del g_ar
         payload = B * H * 2
+        sweep = None if args.no_sweep else allreduce_sweep(comm, rank, world, dev, args.seed)
         fused_ar = {"tokens": B, "payload_bytes": payload, "us": t_ar * 1e6,
                     "bus_gbs": 2 * (world - 1) / world * payload / t_ar / 1e9,
-                    "nvlink_peak_gbs_per_direction": 770.0,
+                    "nvlink_peak_gbs": sweep["nvlink_peak_gbs"] if sweep else None,
+                    "nvlink_peak_source": sweep["nvlink_peak_source"] if sweep else None,
                     "o_proj_gemm_alone_us": kern["o_proj"]["us"],
                     "note": "o_proj GEMM with the reduce-scatter pushed from its epilogue, then the "
                             "reduce + residual + RMSNorm + all-gather kernel"}
@@ -576,11 +905,10 @@ def run_ours(args):
             "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: N(0,0.02) weights, random KV cache, random block-table permutation",
-            "config": {"workload": workload_name(args, world), "model": "llama3-8b-shape", "global_batch": B,
-                       "seq_len": ctx, "parallelism": f"tp{world}",
-                       "l2": "inputs larger than L2 (weights + KV read per step >> 126 MB)"},
+            "config": decode_config(args, world),
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
             "gpu_launches": launches, "kernels": kern, "fused_allreduce": fused_ar,
+            "fused_allreduce_sweep": sweep, "parity": parity,
         }
         print(json.dumps(line), flush=True)
     if comm is not None:
@@ -588,6 +916,9 @@ def run_ours(args):
         comm.cleanup()
     if world > 1:
         dist.destroy_process_group()
+    if parity is not None and not parity["pass"]:
+        print(f"parity check failed at TP={world}: {json.dumps(parity)}", file=sys.stderr)
+        return 1
     return 0
 
 
@@ -839,7 +1170,6 @@ def run_allreduce(args):
     import torch
     import torch.distributed as dist
 
-    from pythonintern_b200 import _lib, kernels
     from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -852,95 +1182,20 @@ def run_allreduce(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
-    H, I = 4096, 14336
-    Tmax = 4096
-    K = I // world
-    comm = DistributedCommunicator(rank, world, device=dev, max_bytes=max(64 << 20, Tmax * H * 2))
+    comm = DistributedCommunicator(rank, world, device=dev, max_bytes=64 << 20)
     comm.connect()
-    g = torch.Generator(device=dev)
-    g.manual_seed(args.seed + 1 + rank)
-    w = (torch.randn(H, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)  # packed [out, in] rows
-    nw = torch.ones(H, device=dev)
-    stream = torch.cuda.current_stream(dev)
-
-    def max_over_ranks(x: float) -> float:
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def time_graph(fn, n, reps=5):
-        """Device seconds per call: n calls captured in one graph, replayed `reps` times, max over ranks."""
-        for _ in range(2):
-            fn()
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr):
-            for _ in range(n):
-                fn()
-        dist.barrier()
-        gr.replay()
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(reps):
-            gr.replay()
-        e1.record(stream)
-        e1.synchronize()
-        del gr
-        return max_over_ranks(e0.elapsed_time(e1) / (reps * n) / 1000.0)
-
-    rows = []
     clocks = ClockSampler(local)
     clocks.start()
-    for T in (1, 8, 64, 512, 4096):
-        x = torch.randn(T, K, device=dev, generator=g).to(torch.bfloat16)
-        r0, r1, R = comm.row_slice(T)
-        h = torch.zeros(R, H, device=dev)
-        y = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
-        n = 20 if T <= 512 else 6  # an even count keeps the exchange slots in step
-
-        def fused():
-            comm.row_parallel_linear(x, w)
-            comm.allreduce_rmsnorm_sharded(T, H, torch.bfloat16, h, nw, 1e-5, out=y)
-        t_fused = time_graph(fused, n)
-        t_gemm = time_graph(lambda: kernels.linear(x, w), n)
-        payload = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
-        for _ in range(3):
-            dist.all_reduce(payload)
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(n):
-            dist.all_reduce(payload)
-        e1.record(stream)
-        e1.synchronize()
-        t_nccl = max_over_ranks(e0.elapsed_time(e1) / n / 1000.0)
-        nbytes = T * H * 2
-        bus = 2 * (world - 1) / world * nbytes
-        rows.append({"tokens": T, "payload_bytes": nbytes, "fused_us": t_fused * 1e6, "gemm_alone_us": t_gemm * 1e6,
-                     "fused_bus_gbs": bus / t_fused / 1e9, "nccl_allreduce_us": t_nccl * 1e6,
-                     "nccl_bus_gbs": bus / t_nccl / 1e9,
-                     "gemm_plus_nccl_us": (t_gemm + t_nccl) * 1e6})
+    sweep = allreduce_sweep(comm, rank, world, dev, args.seed)
     clk = clocks.stop()
-    _lib.check_device_status(dev, "all-reduce microbenchmark")
     if rank == 0:
-        top = rows[-1]
+        top = sweep["sizes"][-1]
         line = {
             "metric": "row-parallel all-reduce bus GB/s", "value": top["fused_bus_gbs"], "unit": "GB/s",
             "n_gpus": world, "steps": None, "warmup": 2, "ms_per_step": top["fused_us"] / 1000.0,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded N(0,1) activations, N(0,0.02) weights",
-            "config": {"workload": (f"row-parallel GEMM [T, {I}/{world}] x [{I}/{world}, {H}] + all-reduce + residual "
-                                    f"+ RMSNorm, TP={world}; value at T=4096"),
-                       "parallelism": f"tp{world}", "tokens": [r["tokens"] for r in rows]},
-            "nvlink_peak_gbs_per_direction": 770.0,
-            "note": ("fused_us includes the GEMM (its epilogue pushes the partial rows); bus GB/s counts the "
-                     "all-reduce payload only, so the GEMM's time lowers it; gemm_plus_nccl_us is the unfused "
-                     "alternative (GEMM, then an NCCL all-reduce, without the residual and RMSNorm)"),
-            "clocks": clk, "sizes": rows,
+            "config": rowpar_config(world), "clocks": clk, **sweep,
         }
         print(json.dumps(line), flush=True)
     dist.barrier()

@@ -1,7 +1,8 @@
 """Generate the golden vectors that pin the oracle to the reference engine.
 
-Runs the UNMODIFIED reference (kmadasamy212-tech/pythonintern, read-only at
-/root/reference) on CPU and writes small fixtures next to this script:
+Runs the UNMODIFIED reference (kmadasamy212-tech/pythonintern, a read-only checkout
+whose path is the first argument or ``$PYTHONINTERN_REFERENCE``) on CPU and writes
+small fixtures next to this script:
 
 * ``tiny_weights_fingerprint.json`` - sha256 of every tensor of the seed-0 Tiny
   LLaMA state dict the reference builds (so the seed-0 weights can be regenerated
@@ -17,7 +18,7 @@ Runs the UNMODIFIED reference (kmadasamy212-tech/pythonintern, read-only at
 The reference's generated protobuf stubs were produced by a newer protoc than the
 installed runtime, so the two version checks are disabled before import.
 
-Usage:  python tests/golden/make_golden.py   (needs /root/reference; CPU only)
+Usage:  python tests/golden/make_golden.py <reference checkout>   (CPU only)
 """
 
 import hashlib
@@ -30,7 +31,11 @@ import threading
 import numpy as np
 import torch
 
-REF = "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PYTHONINTERN_REFERENCE", "")
+if not REF or not os.path.isdir(os.path.join(REF, "engine")):
+    sys.exit("usage: make_golden.py <path to a kmadasamy212-tech/pythonintern checkout> "
+             "(or set PYTHONINTERN_REFERENCE)")
+REF = os.path.abspath(REF)
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.dont_write_bytecode = True

@@ -11,19 +11,22 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 
 
-def test_cpu_sample_small_shape():
+def test_cpu_decode_small_shape_tp1_and_tp2():
+    """The reference-arm timing at a small shape: one rank, then two rank processes over gRPC."""
     import bench
     from pythonintern_b200 import workloads
     cfg = workloads.tinyllama_config(num_layers=2)
     cfg.vocab_size = 1024
-    t = bench.cpu_sample(cfg, batch=2, ctx=64, seed=0)
-    assert 0 < t < 60
+    for world in (1, 2):
+        r = bench.cpu_decode(cfg, world, batch=2, ctx=64, steps=2, warmup=1, seed=0, cores=2)
+        assert len(r["step_s"]) == 2 and all(0 < t < 60 for t in r["step_s"])
+        assert r["threads_used"] == [max(1, 2 // world)] * world
 
 
 def test_reference_arm_prints_one_json_line():
-    env = dict(os.environ, RANK="0")
+    env = dict(os.environ, RANK="0", WORLD_SIZE="1")
     out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
-                          "--warmup", "0", "--cpu-sample-batch", "1", "--ctx", "64"],
+                          "--warmup", "0", "--batch", "2", "--ctx", "64"],
                          capture_output=True, text=True, timeout=600, env=env)
     assert out.returncode == 0, out.stderr
     lines = [l for l in out.stdout.splitlines() if l.strip()]
@@ -31,6 +34,15 @@ def test_reference_arm_prints_one_json_line():
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["value"] > 0 and d["cpu_baseline"]["kind"] == "port"
     assert d["e2e"]["h2d_bytes_per_step"] == 0
+    assert d["cpu_baseline"]["batch"] == 2 and d["cpu_baseline"]["layers_sampled"] == 1
+    assert d["config"]["parallelism"] == "tp1" and d["config"]["global_batch"] == 2
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2")
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--gpus", "2"],
+                         capture_output=True, text=True, timeout=120, env=env)
+    assert out.returncode == 0 and out.stdout.strip() == ""
 
 
 def test_cpu_prefill_sample_and_flop_count():

@@ -187,3 +187,19 @@ def test_tiny_per_layer_activations():
     model.forward(np.asarray([prompts[0]]), np.arange(len(prompts[0]))[None], [table], True, trace=trace)
     for layer in range(4):
         assert rel(trace[layer][0], gold["prefill_trace"][layer]) < 1e-5
+
+
+def test_tp_parity_fixture_matches_oracle():
+    """The Llama-3-8B-shape layer fixture that bench.py's parity leg reads is what the oracle
+    computes (float16 storage of the hidden states: relative rounding <= 2**-11)."""
+    import importlib.util
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "make_tp_parity.py")
+    spec = importlib.util.spec_from_file_location("make_tp_parity", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    want = mod.compute()
+    got = np.load(mod.OUT)
+    for k in ("prompt0", "prompt1", "tokens"):
+        assert np.array_equal(got[k], want[k]), k
+    for k in ("hidden_prefill", "hidden_decode", "logits", "margins"):
+        assert np.allclose(got[k].astype(np.float64), want[k].astype(np.float64), rtol=1e-3, atol=1e-3), k

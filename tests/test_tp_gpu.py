@@ -6,6 +6,9 @@
 * The Tiny LLaMA workload at TP=2 with one process per GPU: greedy tokens identical to
   the reference's TP=2 run.
 * A Llama-3-8B-shape bf16 layer at TP=2 against the oracle.
+* bench.py's parity leg at TP = 1, 2, 4 and 8 (an 8B-shape layer against the oracle
+  fixture, greedy tokens, and at TP <= 2 the Tiny LLaMA tokens of the reference).
+* The decode-step sharded all-reduce and the module-level all-reduce at 4 and 8 ranks.
 * The timeout path on ONE GPU: rank 1 joins but never enters the all-reduce; rank 0's
   bounded wait runs out and surfaces as TimeoutError (no GPU fault, only rank 0 waits).
 Multi-GPU cases skip when fewer GPUs are visible.
@@ -119,25 +122,73 @@ def test_sharded_allreduce_rmsnorm_more_rows_than_ctas():
         c.cleanup()
 
 
-@pytest.mark.skipif(NGPU < 4, reason="needs 4 GPUs")
-def test_all_reduce_4_ranks():
+@pytest.mark.parametrize("world", [4, 8])
+def test_all_reduce_4_and_8_ranks(world):
+    if NGPU < world:
+        pytest.skip(f"needs {world} GPUs")
     from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
-    comms = [DistributedCommunicator(rank=r, world_size=4, device=f"cuda:{r}") for r in range(4)]
-    for i in range(4):
-        for j in range(4):
+    comms = [DistributedCommunicator(rank=r, world_size=world, device=f"cuda:{r}") for r in range(world)]
+    for i in range(world):
+        for j in range(world):
             if i != j:
                 comms[i].register_in_memory_peer(j, comms[j])
-    res = [None] * 4
+    res = [None] * world
 
     def run(r):
         with torch.cuda.device(r):
             t = torch.full((2, 8), float(r + 1), device=f"cuda:{r}")
             res[r] = comms[r].all_reduce_sum(t, step_tag="step_test_collectives").cpu()
-    th = [threading.Thread(target=run, args=(r,)) for r in range(4)]
+    th = [threading.Thread(target=run, args=(r,)) for r in range(world)]
     [t.start() for t in th]
     [t.join() for t in th]
-    for r in range(4):
-        assert torch.equal(res[r], torch.full((2, 8), 10.0))
+    for r in range(world):
+        assert torch.equal(res[r], torch.full((2, 8), float(world * (world + 1) // 2)))
+    for c in comms:
+        c.cleanup()
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_sharded_allreduce_rmsnorm_decode_rows_4_and_8_ranks(world):
+    """The decode-step exchange at 4 and 8 ranks: 128 rows of hidden 4096 (the bench's batch),
+    every rank pushing its partial rows, three calls in a row (the receive slots rotate),
+    against torch float32 on the same inputs; every rank gets identical normalised rows."""
+    if NGPU < world:
+        pytest.skip(f"needs {world} GPUs")
+    from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
+    T, K, H, eps = 128, 64 * world, 4096, 1e-5
+    gen = torch.Generator().manual_seed(11)
+    comms = [DistributedCommunicator(rank=r, world_size=world, device=f"cuda:{r}") for r in range(world)]
+    for i in range(world):
+        for j in range(world):
+            if i != j:
+                comms[i].register_in_memory_peer(j, comms[j])
+    for call in range(3):
+        x = torch.randn(T, K, generator=gen).to(torch.bfloat16)
+        w = (torch.randn(K, H, generator=gen) * 0.05).to(torch.bfloat16)
+        resid = torch.randn(T, H, generator=gen)
+        nw = torch.rand(H, generator=gen) + 0.5
+        hs = resid + x.float() @ w.float()
+        want = hs * torch.rsqrt(hs.pow(2).mean(-1, keepdim=True) + eps) * nw
+        out = [None] * world
+        kk = K // world
+
+        def run(r):
+            dev = f"cuda:{r}"
+            with torch.cuda.device(r):
+                wr = w[r * kk:(r + 1) * kk].t().contiguous().to(dev)  # packed [out, in] rows
+                r0, r1, R = comms[r].row_slice(T)
+                h = torch.zeros(R, H, device=dev)
+                h[: r1 - r0] = resid[r0:r1].to(dev)
+                comms[r].row_parallel_linear(x[:, r * kk:(r + 1) * kk].contiguous().to(dev), wr)
+                y = comms[r].allreduce_rmsnorm_sharded(T, H, torch.bfloat16, h, nw.to(dev), eps)
+                torch.cuda.synchronize()
+                out[r] = y.float().cpu()
+        th = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+        [t.start() for t in th]
+        [t.join() for t in th]
+        for r in range(world):
+            assert float((out[r] - want).norm() / want.norm()) < 2e-2, (call, r)
+            assert torch.equal(out[r], out[0])
     for c in comms:
         c.cleanup()
 
@@ -289,6 +340,57 @@ def test_llama3_8b_shape_layer_tp2_matches_oracle(tmp_path):
     om.forward(toks.numpy(), np.arange(40)[None], [[3, 9, 1]], True, trace=otr)
     err = np.linalg.norm(h0 - otr[0][0]) / np.linalg.norm(otr[0][0])
     assert err < 2e-2
+
+
+# ------------------------------------------------------------------ bench.py's parity leg at TP = 1, 2, 4, 8
+def _parity_worker(rank, world, port, out_dir):
+    import json
+    import sys
+    sys.path.insert(0, ROOT)
+    import torch.distributed as dist
+    from datetime import timedelta
+    import bench
+    from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=120), device_id=dev)
+    comm = DistributedCommunicator(rank, world, device=dev, max_bytes=64 << 20).connect()
+    res = bench.tp_parity(comm, rank, world, dev)
+    with open(os.path.join(out_dir, f"parity_rank{rank}.json"), "w") as f:
+        json.dump(res, f)
+    dist.barrier()
+    comm.cleanup()
+    dist.destroy_process_group()
+
+
+def test_parity_leg_tp1():
+    """The 8B-shape layer against the oracle fixture and the Tiny LLaMA tokens against the
+    reference's golden, at TP=1 (bench.py runs this before timing)."""
+    import sys
+    sys.path.insert(0, ROOT)
+    import bench
+    res = bench.tp_parity(None, 0, 1, torch.device("cuda", 0))
+    assert res["pass"], res
+    assert res["layer_rel_err"] < 2e-2 and res["tokens_checked"] >= 4 and res["tiny_tokens_match"]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_parity_leg_multi_gpu(world, tmp_path):
+    """The same check at TP = 2, 4 and 8, one process per GPU (NCCL for the bench's bookkeeping,
+    the row-parallel exchange over NVLink peer memory)."""
+    import json
+    if NGPU < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.start_processes(_parity_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    res = [json.loads((tmp_path / f"parity_rank{r}.json").read_text()) for r in range(world)]
+    for r in res:
+        assert r == res[0]
+    assert res[0]["pass"], res[0]
+    assert res[0]["layer_rel_err"] < 2e-2 and res[0]["tokens_checked"] >= 4 and res[0]["ranks_agree"]
+    if world == 2:
+        assert res[0]["tiny_tokens_match"] is True
 
 
 # ------------------------------------------------------------------ timeout on one GPU
