@@ -416,8 +416,8 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnP
   const char* vbase = reinterpret_cast<const char*>(p.v_cache) + (p.layer_off + (int64_t)g * HD) * 2;
   const uint32_t wsm = smem_addr(smem) + (uint32_t)(warp * kMmaStages * C::STAGEB);
 
-  // Issue the copies of this warp's i-th block into ring slot (i % STAGES); returns false
-  // for a block id outside the pool (its scores are then masked).
+  // Issue the copies of this warp's i-th block into ring slot (i % STAGES); a block id
+  // outside the pool is not copied, and the main loop skips that block.
   auto issue = [&](int i) {
     const int blk = table[blk0 + warp + i * kMmaWarps];
     if (blk < 0 || blk >= p.num_blocks) return;
@@ -450,7 +450,13 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnP
     const int bidx = blk0 + warp + i * kMmaWarps;
     const int blk = table[bidx];
     const bool blk_ok = blk >= 0 && blk < p.num_blocks;
-    if (!blk_ok && lane == 0) raise_status(p.status, B2_DEV_RANGE);
+    if (!blk_ok) {
+      // Nothing was copied into this ring slot: skip the block entirely (scores AND the PV
+      // product), so stale shared memory never reaches the output.
+      if (lane == 0) raise_status(p.status, B2_DEV_RANGE);
+      __syncwarp();
+      continue;
+    }
     const uint32_t ks = wsm + (uint32_t)((i % kMmaStages) * C::STAGEB);
     const uint32_t vs = ks + C::BLKB;
 
@@ -671,7 +677,7 @@ __global__ void __launch_bounds__(kPfWarps * 32) prefill_attn_mma_kernel(Prefill
 
   auto block_id = [&](int b) -> int { return b < p.table_stride ? table[b] : -1; };
   // All threads copy block b (K and V rows of this kv head) into ring slot b % kPfStages;
-  // a block id outside the pool is not read (its scores are masked).
+  // a block id outside the pool is not read, and the main loop skips that block.
   auto issue = [&](int b) {
     const int blk = block_id(b);
     if (blk < 0 || blk >= p.num_blocks) return;
@@ -703,7 +709,9 @@ __global__ void __launch_bounds__(kPfWarps * 32) prefill_attn_mma_kernel(Prefill
     const int blk = block_id(b);
     const bool blk_ok = blk >= 0 && blk < p.num_blocks;
     if (!blk_ok && threadIdx.x == 0) raise_status(p.status, B2_DEV_RANGE);
-    if (b * 16 > wpos) continue;  // every key of the block follows every row of this warp
+    // An out-of-range block was not copied (its ring slot is stale): skip it whole, like a
+    // block whose every key follows every row of this warp.
+    if (!blk_ok || b * 16 > wpos) continue;
     const uint32_t ks = sbase + (uint32_t)((b % kPfStages) * C::STAGEB);
     const uint32_t vs = ks + C::BLKB;
 
@@ -923,6 +931,35 @@ static int noalloc_scratch(void** out) {
   return B2_OK;
 }
 
+// Argument checks shared by b2_paged_attention and b2_paged_attention_noalloc (the
+// latter runs them before it touches its shared scratch).  Workspace size is checked
+// by the caller that owns the workspace.
+static int check_paged_args(const void* q, int64_t ld_q, int n_rows, int nq, int nkv, int head_dim,
+                            const void* k_cache, const void* v_cache, int layer, int num_blocks, int block_size,
+                            const int32_t* block_tables, int table_stride, const int32_t* ctx_lens, void* out,
+                            int64_t ld_out, int dtype, int num_splits) {
+  B2_CHECK_ARG(n_rows >= 0 && nq > 0 && nkv > 0 && nq % nkv == 0, "b2_paged_attention: bad head counts");
+  B2_CHECK_ARG(valid_dtype(dtype), "b2_paged_attention: bad dtype");
+  B2_CHECK_ARG(num_blocks > 0 && block_size > 0 && table_stride > 0 && layer >= 0,
+               "b2_paged_attention: bad cache geometry");
+  B2_CHECK_ARG(num_splits >= 1 && num_splits <= 1024, "b2_paged_attention: num_splits %d out of [1, 1024]", num_splits);
+  B2_CHECK_ARG(ld_q >= (int64_t)nq * head_dim && ld_out >= (int64_t)nq * head_dim,
+               "b2_paged_attention: row strides too small");
+  if (n_rows == 0) return B2_OK;
+  B2_CHECK_ARG(q && k_cache && v_cache && block_tables && ctx_lens && out, "b2_paged_attention: null pointer");
+  B2_CHECK_ARG(n_rows <= 65535, "b2_paged_attention: n_rows %d > 65535", n_rows);
+  const size_t esz = dtype_bytes(dtype);
+  B2_CHECK_ARG(((uintptr_t)q % 16) == 0 && ((ld_q * esz) % 16) == 0 && ((uintptr_t)k_cache % 16) == 0 &&
+                   ((uintptr_t)v_cache % 16) == 0,
+               "b2_paged_attention: q/cache must be 16-byte aligned");
+  if (num_splits > 1)
+    B2_CHECK_ARG((size_t)n_rows * nkv <= kAttnCounterSlots,
+                 "b2_paged_attention: n_rows * nkv = %d exceeds %zu with num_splits > 1", n_rows * nkv,
+                 kAttnCounterSlots);
+  if (dtype == B2_BF16) B2_CHECK_ARG(block_size == 16, "b2_paged_attention: bf16 path needs block_size 16");
+  return B2_OK;
+}
+
 }  // namespace b2
 
 extern "C" {
@@ -937,26 +974,12 @@ int b2_paged_attention(const void* q, int64_t ld_q, int n_rows, int nq, int nkv,
                        const int32_t* table_index, const int32_t* ctx_lens, int compat_pad,
                        float scale, void* out, int64_t ld_out, int dtype, void* workspace,
                        size_t workspace_bytes, int num_splits, int32_t* status, b2_stream_t stream) {
-  B2_CHECK_ARG(n_rows >= 0 && nq > 0 && nkv > 0 && nq % nkv == 0, "b2_paged_attention: bad head counts");
-  B2_CHECK_ARG(b2::valid_dtype(dtype), "b2_paged_attention: bad dtype");
-  B2_CHECK_ARG(num_blocks > 0 && block_size > 0 && table_stride > 0 && layer >= 0,
-               "b2_paged_attention: bad cache geometry");
-  B2_CHECK_ARG(num_splits >= 1 && num_splits <= 1024, "b2_paged_attention: num_splits %d out of [1, 1024]", num_splits);
-  B2_CHECK_ARG(ld_q >= (int64_t)nq * head_dim && ld_out >= (int64_t)nq * head_dim,
-               "b2_paged_attention: row strides too small");
-  if (n_rows == 0) return B2_OK;
-  B2_CHECK_ARG(q && k_cache && v_cache && block_tables && ctx_lens && out, "b2_paged_attention: null pointer");
-  B2_CHECK_ARG(n_rows <= 65535, "b2_paged_attention: n_rows %d > 65535", n_rows);
-  const size_t esz = b2::dtype_bytes(dtype);
-  B2_CHECK_ARG(((uintptr_t)q % 16) == 0 && ((ld_q * esz) % 16) == 0 && ((uintptr_t)k_cache % 16) == 0 &&
-                   ((uintptr_t)v_cache % 16) == 0,
-               "b2_paged_attention: q/cache must be 16-byte aligned");
+  const int rc = b2::check_paged_args(q, ld_q, n_rows, nq, nkv, head_dim, k_cache, v_cache, layer, num_blocks,
+                                     block_size, block_tables, table_stride, ctx_lens, out, ld_out, dtype, num_splits);
+  if (rc != B2_OK || n_rows == 0) return rc;
   b2::AttnWs lay = b2::attn_ws_layout(n_rows, nq, nkv, head_dim, num_splits);
   b2::AttnParams p{};
   if (num_splits > 1) {
-    B2_CHECK_ARG((size_t)n_rows * nkv <= b2::kAttnCounterSlots,
-                 "b2_paged_attention: n_rows * nkv = %d exceeds %zu with num_splits > 1", n_rows * nkv,
-                 b2::kAttnCounterSlots);
     B2_CHECK_ARG(workspace && workspace_bytes >= lay.total,
                  "b2_paged_attention: workspace of %zu bytes needed, %zu given", lay.total, workspace_bytes);
     char* ws = static_cast<char*>(workspace);
@@ -986,10 +1009,7 @@ int b2_paged_attention(const void* q, int64_t ld_q, int n_rows, int nq, int nkv,
   p.status = status;
   dim3 grid(num_splits, nkv, n_rows);
   const int rep = nq / nkv;
-  if (dtype == B2_BF16) {
-    B2_CHECK_ARG(block_size == 16, "b2_paged_attention: bf16 path needs block_size 16");
-    return b2::launch_mma(head_dim, rep, p, grid, stream);
-  }
+  if (dtype == B2_BF16) return b2::launch_mma(head_dim, rep, p, grid, stream);
   return b2::launch_hd<float>(head_dim, rep, p, grid, stream);
 }
 
@@ -1001,19 +1021,22 @@ int b2_paged_attention_noalloc(const void* q, int64_t ld_q, int n_rows, int nq, 
                                const int32_t* table_index, const int32_t* ctx_lens, int compat_pad,
                                float scale, void* out, int64_t ld_out, int dtype, int num_splits,
                                int32_t* status, b2_stream_t stream) {
+  // Every argument is checked before the shared scratch is touched: a rejected call must
+  // not clear counters that a call still running on another stream is using.
+  int rc = b2::check_paged_args(q, ld_q, n_rows, nq, nkv, head_dim, k_cache, v_cache, layer, num_blocks, block_size,
+                                block_tables, table_stride, ctx_lens, out, ld_out, dtype, num_splits);
+  if (rc != B2_OK || n_rows == 0) return rc;
   void* scratch = nullptr;
   if (num_splits > 1) {
-    B2_CHECK_ARG(n_rows >= 0 && nq > 0 && nkv > 0 && head_dim > 0 && num_splits <= 1024,
-                 "b2_paged_attention_noalloc: bad sizes");
     const size_t need = b2_paged_attention_workspace_bytes(n_rows, nq, nkv, head_dim, num_splits);
     B2_CHECK_ARG(need <= b2::kNoAllocScratchBytes,
                  "b2_paged_attention_noalloc: this call needs %zu bytes of split scratch but the static "
                  "array holds %zu; use fewer splits or rows, or b2_paged_attention with a workspace",
                  need, b2::kNoAllocScratchBytes);
-    const int rc = b2::noalloc_scratch(&scratch);
+    rc = b2::noalloc_scratch(&scratch);
     if (rc) return rc;
     // The array keeps the previous call's contents: zero the split counters this call uses.
-    if (n_rows > 0) B2_TRY_CUDA(cudaMemsetAsync(scratch, 0, (size_t)n_rows * nkv * sizeof(int), stream));
+    B2_TRY_CUDA(cudaMemsetAsync(scratch, 0, (size_t)n_rows * nkv * sizeof(int), stream));
   }
   return b2_paged_attention(q, ld_q, n_rows, nq, nkv, head_dim, k_cache, v_cache, layer, num_blocks, block_size,
                             block_tables, table_stride, table_index, ctx_lens, compat_pad, scale, out, ld_out,

@@ -203,3 +203,14 @@ def test_tp_parity_fixture_matches_oracle():
         assert np.array_equal(got[k], want[k]), k
     for k in ("hidden_prefill", "hidden_decode", "logits", "margins"):
         assert np.allclose(got[k].astype(np.float64), want[k].astype(np.float64), rtol=1e-3, atol=1e-3), k
+
+
+def test_package_rope_tables_bit_exact(units):
+    """The tables the CUDA path uploads (pythonintern_b200.model.attention.RotaryEmbedding, built on
+    the host) equal the reference's own tables bit for bit at head_dim 32, 64 and 128."""
+    from pythonintern_b200.model.attention import RotaryEmbedding
+    for hd in (32, 64, 128):
+        rope = RotaryEmbedding(hd, max_seq_len=2048, device="cpu")
+        rows = units[f"rope{hd}_rows"]
+        assert np.array_equal(rope.cos_cached[rows].numpy(), units[f"rope{hd}_cos"]), hd
+        assert np.array_equal(rope.sin_cached[rows].numpy(), units[f"rope{hd}_sin"]), hd

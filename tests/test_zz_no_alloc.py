@@ -28,7 +28,7 @@ from pythonintern_b200 import _lib, kernels  # noqa: E402
 DEV = torch.device("cuda", 0)
 
 
-def _case(seed):
+def _case(seed, dtype=torch.float32):
     gen = torch.Generator().manual_seed(seed)
     B, nq, nkv, hd, bs = 6, 32, 8, 128, 16
     ctxs = [700, 1, 333, 64, 1024, 129]
@@ -40,9 +40,9 @@ def _case(seed):
     for b, n in enumerate(nblk):
         tab[b, :n] = perm[k:k + n]
         k += n
-    kc = torch.randn(2, NB, bs, nkv, hd, generator=gen).to(DEV)
-    vc = torch.randn(2, NB, bs, nkv, hd, generator=gen).to(DEV)
-    q = torch.randn(B, nq * hd, generator=gen).to(DEV)
+    kc = torch.randn(2, NB, bs, nkv, hd, generator=gen).to(dtype).to(DEV)
+    vc = torch.randn(2, NB, bs, nkv, hd, generator=gen).to(dtype).to(DEV)
+    q = torch.randn(B, nq * hd, generator=gen).to(dtype).to(DEV)
     return q, kc, vc, torch.from_numpy(tab).to(DEV), torch.tensor(ctxs, dtype=torch.int32, device=DEV), nq, nkv, hd
 
 
@@ -51,7 +51,28 @@ def _noalloc(q, kc, vc, tab, ctx, nq, nkv, hd, splits, out):
     return _lib.lib().b2_paged_attention_noalloc(
         q.data_ptr(), q.stride(0), q.shape[0], nq, nkv, hd, kc.data_ptr(), vc.data_ptr(), 1, NB, bs,
         tab.data_ptr(), tab.shape[1], None, ctx.data_ptr(), 1, 1.0 / math.sqrt(hd), out.data_ptr(), out.stride(0),
-        _lib.B2_F32, splits, _lib.status_ptr(DEV), _lib.stream_ptr(DEV))
+        _lib.B2_BF16 if q.dtype == torch.bfloat16 else _lib.B2_F32, splits, _lib.status_ptr(DEV),
+        _lib.stream_ptr(DEV))
+
+
+def _torch_reference(q, kc, vc, tab, ctx, nq, nkv, hd):
+    """float32 decode attention of layer 1 with the reference's unmasked zero padding: every row
+    also counts (max_ctx - ctx) zero scores in its softmax denominator (attention.py:190-224)."""
+    q, kc, vc = q.float().cpu(), kc.float().cpu(), vc.float().cpu()
+    tab, ctx = tab.cpu(), ctx.cpu().tolist()
+    L = max(ctx)
+    rep = nq // nkv
+    out = torch.zeros(q.shape[0], nq * hd)
+    for b, c in enumerate(ctx):
+        ids = [int(t) for t in tab[b][: (c + 15) // 16]]
+        k = kc[1, ids].reshape(-1, nkv, hd)[:c]
+        v = vc[1, ids].reshape(-1, nkv, hd)[:c]
+        for h in range(nq):
+            s = (k[:, h // rep] @ q[b, h * hd:(h + 1) * hd]) / math.sqrt(hd)
+            s = torch.cat([s, torch.zeros(L - c)])
+            p = torch.softmax(s, 0)[:c]
+            out[b, h * hd:(h + 1) * hd] = p @ v[:, h // rep]
+    return out
 
 
 def rel(a, b):
@@ -71,6 +92,48 @@ def test_noalloc_matches_workspace_entry_point_twice(splits):
         torch.cuda.synchronize()
         _lib.check_device_status(DEV, "noalloc attention")
         assert rel(out, want) < 1e-5  # the float32 attention tolerance of test_kernels_gpu.py
+
+
+def test_noalloc_bf16_split_path_against_torch_and_allocates_nothing():
+    """The bf16 path the model runs (tensor-core kernel, block size 16) with splits > 1:
+    bit-identical to the workspace entry point, within the bf16 attention tolerance of an
+    independent float32 torch computation, on two calls in a row, and neither torch's
+    allocator nor the device's free memory moves across those calls (the first call on the
+    device, made before the measurement, may load the library's module)."""
+    splits = 5
+    q, kc, vc, tab, ctx, nq, nkv, hd = _case(9, torch.bfloat16)
+    want_ws = kernels.paged_attention(q, nq, nkv, hd, kc, vc, 1, tab, None, ctx, True, 1.0 / math.sqrt(hd),
+                                      num_splits=splits)
+    want = _torch_reference(q, kc, vc, tab, ctx, nq, nkv, hd)
+    outs = [torch.full_like(want_ws, float("nan")) for _ in range(3)]
+    assert _noalloc(q, kc, vc, tab, ctx, nq, nkv, hd, splits, outs[0]) == _lib.B2_OK, _lib.last_error()
+    torch.cuda.synchronize()
+    alloc0 = torch.cuda.memory_allocated(DEV)
+    free0 = torch.cuda.mem_get_info(DEV)[0]
+    for out in outs[1:]:
+        rc = _noalloc(q, kc, vc, tab, ctx, nq, nkv, hd, splits, out)
+        assert rc == _lib.B2_OK, _lib.last_error()
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated(DEV) == alloc0
+    assert torch.cuda.mem_get_info(DEV)[0] == free0
+    _lib.check_device_status(DEV, "noalloc attention bf16")
+    for out in outs:
+        assert torch.equal(out, want_ws)
+        assert rel(out, want) < 1e-2  # the bf16 attention tolerance of test_kernels_gpu.py
+
+
+def test_noalloc_rejects_bad_arguments():
+    """Bad arguments are rejected with the same checks as b2_paged_attention (the entry point
+    runs them before it clears any shared counter, so a rejected call cannot disturb a call
+    still running on another stream)."""
+    q, kc, vc, tab, ctx, nq, nkv, hd = _case(2)
+    out = torch.empty_like(q)
+    bad_rows = 70000  # over the 65535-row limit: rejected by the argument checks
+    rc = _lib.lib().b2_paged_attention_noalloc(
+        q.data_ptr(), q.stride(0), bad_rows, nq, nkv, hd, kc.data_ptr(), vc.data_ptr(), 1, kc.shape[1], 16,
+        tab.data_ptr(), tab.shape[1], None, ctx.data_ptr(), 1, 0.1, out.data_ptr(), out.stride(0), _lib.B2_F32, 4,
+        _lib.status_ptr(DEV), _lib.stream_ptr(DEV))
+    assert rc == _lib.B2_EINVAL and "65535" in _lib.last_error()
 
 
 def test_noalloc_rejects_calls_beyond_its_scratch():
