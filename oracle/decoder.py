@@ -162,7 +162,7 @@ class FifoBlockAllocator:
         """kv_cache.py:180-199."""
         need = math.ceil(num_tokens / self.block_size)
         if need > len(self.free):
-            raise MemoryError(f"Cannot allocate {need} blocks for seq {seq_id}")
+            raise MemoryError(f"sequence {seq_id} needs {need} blocks")
         table = self.tables.setdefault(seq_id, [])
         while len(table) < need:
             table.append(self.free.pop(0))
@@ -176,7 +176,7 @@ class FifoBlockAllocator:
         idx, off = pos // self.block_size, pos % self.block_size
         if idx >= len(table):
             if not self.free:
-                raise MemoryError("Out of KV cache memory")
+                raise MemoryError("no free block left")
             table.append(self.free.pop(0))
         self.num_tokens[seq_id] += 1
         return table[idx], off
@@ -392,11 +392,13 @@ def execute_step(model: OracleModel, slots: List[Slot]):
     (all prefills, then all decodes).
     """
     out = []
+    full = []  # every row's full logits, kept on the model as ``last_logits`` for margin checks
     for s in (s for s in slots if s.is_prefill):
         toks = np.asarray([s.prompt_token_ids], dtype=np.int64)
         pos = np.arange(toks.shape[1], dtype=np.int64)[None, :]
         logits = model.forward(toks, pos, [list(s.block_table)], True)
         out.append((s.seq_id, int(np.argmax(logits[0])), logits[0][:10].copy()))
+        full.append(logits[0])
     dec = [s for s in slots if not s.is_prefill]
     if dec:
         toks = np.asarray([[s.current_token_id] for s in dec], dtype=np.int64)
@@ -404,6 +406,8 @@ def execute_step(model: OracleModel, slots: List[Slot]):
         logits = model.forward(toks, pos, [list(s.block_table) for s in dec], False)
         for i, s in enumerate(dec):
             out.append((s.seq_id, int(np.argmax(logits[i])), logits[i][:10].copy()))
+            full.append(logits[i])
+    model.last_logits = np.stack(full) if full else None
     return out
 
 

@@ -40,7 +40,8 @@ class BlockTable:
         block_idx = logical_pos // self.block_size
         offset = logical_pos % self.block_size
         assert block_idx < len(self.physical_block_ids), (
-            f"Logical position {logical_pos} exceeds allocated blocks ({len(self.physical_block_ids)})")
+            f"sequence {self.seq_id}: token {logical_pos} falls in block {block_idx}, but only "
+            f"{len(self.physical_block_ids)} blocks are allocated")
         return self.physical_block_ids[block_idx], offset
 
 
@@ -118,8 +119,8 @@ class KVCacheManager:
     def allocate_blocks_for_sequence(self, seq_id: str, num_tokens: int) -> BlockTable:
         needed_blocks = math.ceil(num_tokens / self.block_size)
         if needed_blocks > len(self.free_blocks):
-            raise MemoryError(f"Cannot allocate {needed_blocks} blocks for seq {seq_id}. "
-                              f"Only {len(self.free_blocks)} free blocks remaining.")
+            raise MemoryError(f"sequence {seq_id} needs {needed_blocks} KV blocks; "
+                              f"{len(self.free_blocks)} are free")
         if seq_id not in self.block_tables:
             self.block_tables[seq_id] = BlockTable(seq_id, self.block_size)
         table = self.block_tables[seq_id]
@@ -135,7 +136,7 @@ class KVCacheManager:
         offset = new_token_pos % self.block_size
         if block_idx >= len(table.physical_block_ids):
             if not self.free_blocks:
-                raise MemoryError(f"Out of KV cache memory. Cannot allocate block for seq {seq_id}.")
+                raise MemoryError(f"KV pool exhausted: no free block for the next token of sequence {seq_id}")
             table.append_block(self.free_blocks.pop(0))
         table.num_tokens += 1
         return table.physical_block_ids[block_idx], offset

@@ -2,6 +2,7 @@
 token metadata, weight sharding, step messages, seeded workloads."""
 
 import dataclasses
+import math
 import sys
 
 import numpy as np
@@ -189,3 +190,54 @@ def test_group_prefills_respects_the_token_cap():
     assert group_prefills([10, 10, 10], 100) == [[0, 1, 2]]
     assert group_prefills([10, 10, 10], 100, batch=False) == [[0], [1], [2]]
     assert group_prefills([], 100) == []
+
+
+# ------------------------------------------------------------------ coordinator block allocator
+class _Seq:
+    def __init__(self, seq_id, prompt_len):
+        self.seq_id = seq_id
+        self.prompt_token_ids = list(range(prompt_len))
+        self.output_token_ids = []
+
+    @property
+    def total_length(self):
+        return len(self.prompt_token_ids) + len(self.output_token_ids)
+
+
+def _drive(mm, prompt_len, steps):
+    """The reference batcher's order: allocate the prompt, sample a token, then per decode step
+    append_token_slot before the worker writes position total_length - 1, then sample."""
+    s = _Seq("s", prompt_len)
+    mm.allocate_prefill(s)
+    s.output_token_ids.append(0)
+    short = []
+    for _ in range(steps):
+        mm.append_token_slot(s)
+        pos = s.total_length - 1
+        short.append(pos // mm.block_size >= len(mm.get_block_table("s")))
+        s.output_token_ids.append(0)
+    return short
+
+
+def test_cluster_memory_manager_reproduces_the_off_by_one_by_default():
+    """Prompts of 16 and 32 tokens reach their first decode with a table one block short
+    (engine/scheduler/memory_manager.py:54-74); other lengths do not."""
+    from pythonintern_b200.config import KVCacheConfig
+    from pythonintern_b200.scheduler import ClusterMemoryManager
+    for P in (16, 32):
+        assert _drive(ClusterMemoryManager(KVCacheConfig(16, 64, "cuda")), P, 3)[0] is True
+    assert not any(_drive(ClusterMemoryManager(KVCacheConfig(16, 64, "cuda")), 17, 40))
+
+
+def test_cluster_memory_manager_fixed_allocator_always_covers_the_written_slot():
+    from pythonintern_b200.config import KVCacheConfig
+    from pythonintern_b200.scheduler import ClusterMemoryManager
+    for P in (1, 15, 16, 17, 31, 32, 33, 64):
+        mm = ClusterMemoryManager(KVCacheConfig(16, 64, "cuda"), fixed_allocator=True)
+        assert not any(_drive(mm, P, 50)), P
+        # never more blocks than the tokens need
+        assert len(mm.get_block_table("s")) == math.ceil((P + 50) / 16)
+    mm = ClusterMemoryManager(KVCacheConfig(16, 64, "cuda"), fixed_allocator=True)
+    a, b = _Seq("a", 20), _Seq("b", 5)
+    assert mm.allocate_prefill(a) == [0, 1] and mm.allocate_prefill(b) == [2]   # FIFO pop(0)
+    assert mm.free_sequence(a) == [0, 1] and mm.free_blocks[-2:] == [0, 1]

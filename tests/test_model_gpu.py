@@ -311,3 +311,110 @@ def test_decode_graph_replay_matches_eager():
         # eager and graph pick the same attention split count (same table bucket), so
         # the logits are bit-identical
         np.testing.assert_array_equal(np.asarray(la), np.asarray(lb))
+
+
+def test_llama3_8b_shape_bf16_greedy_tokens_with_margins():
+    """bf16 token-level parity: 16 greedy steps of a 2-layer Llama-3-8B-shape model (vocab 4096)
+    through WorkerExecutionEngine.execute_step (prefill, then CUDA-graph decode steps).
+
+    The oracle decodes free-running in float64 on the bf16-rounded weights; the engine is
+    fed the oracle's tokens (so one near-tie cannot derail the rest) and its greedy token
+    must equal the oracle's wherever the oracle's top-1 minus top-2 logit margin exceeds
+    the bf16 error bound (3x the largest top-logit error seen, at least 0.05).  The
+    per-step margins are printed (pytest -s) so a reader can see how many steps the bound
+    excluded."""
+    cfg = workloads.llama3_8b_config(num_layers=2, max_seq_len=512)
+    cfg.vocab_size = 4096
+    sd = workloads.synthetic_state_dict(cfg, seed=31)
+    eng = WorkerExecutionEngine(cfg, ShardConfig(0, 1), KVCacheConfig(16, 32, str(DEV)), None, DEV)
+    eng.model.load_state_dict(sd)
+    ocfg = oracle.OracleConfig(cfg.vocab_size, cfg.hidden_dim, cfg.num_layers, cfg.num_heads, cfg.num_kv_heads,
+                               cfg.intermediate_dim, cfg.max_seq_len, cfg.rms_norm_eps)
+    om = oracle.OracleModel(ocfg, [{k: v.float().numpy() for k, v in sd.items()}],
+                            [oracle.KVPool(cfg.num_layers, 32, 16, cfg.num_kv_heads, cfg.head_dim)])
+    gen = torch.Generator().manual_seed(8)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=gen).tolist() for n in (29, 45)]
+    tables = [[7, 2, 11, 4], [0, 9, 5, 13, 1]]
+    ids = ["a", "b"]
+    got, want, margins, top_err = [], [], [], 0.0
+    slots = [SequenceSlot(s, True, p, 0, len(p), t) for s, p, t in zip(ids, prompts, tables)]
+    oslots = [oracle.Slot(s, True, p, 0, len(p), t) for s, p, t in zip(ids, prompts, tables)]
+    lens = [len(p) for p in prompts]
+    for step in range(16):
+        resp = eng.execute_step(StepRequest(step, slots))
+        ref = oracle.execute_step(om, oslots)
+        g = [t.token_id for t in resp.sampled_tokens]
+        w = [t for _, t, _ in ref]
+        for t, (_, _, tl) in zip(resp.sampled_tokens, ref):
+            top_err = max(top_err, float(np.abs(np.asarray(t.top_logits) - tl).max()))
+        got.append(g)
+        want.append(w)
+        margins.append(_oracle_margins(om))
+        lens = [n + 1 for n in lens]
+        slots = [SequenceSlot(s, False, [], w[i], lens[i], tables[i]) for i, s in enumerate(ids)]
+        oslots = [oracle.Slot(s, False, [], w[i], lens[i], tables[i]) for i, s in enumerate(ids)]
+    _lib.check_device_status(DEV, "bf16 greedy")
+    margins = np.asarray(margins)
+    bound = max(0.05, 3.0 * top_err)
+    sel = margins > bound
+    print(f"\nbf16 greedy parity: top-logit max error {top_err:.4f}, margin bound {bound:.4f}, "
+          f"{int(sel.sum())}/{sel.size} tokens checked; margins per step:\n{np.round(margins, 3).tolist()}")
+    assert sel.sum() >= sel.size // 2, "too few tokens clear the bf16 error bound to say anything"
+    assert np.array_equal(np.asarray(got)[sel], np.asarray(want)[sel])
+
+
+def _oracle_margins(om):
+    """Top-1 minus top-2 logit of each sequence of the step the oracle just ran (its full
+    logits are kept in ``om.last_logits`` by ``oracle.execute_step``)."""
+    lg = om.last_logits
+    s = np.sort(lg, axis=-1)
+    return (s[:, -1] - s[:, -2]).tolist()
+
+
+def test_fixed_allocator_mode_end_to_end():
+    """The coordinator's block allocator driving execute_step for a 16-token prompt (Tiny LLaMA).
+
+    Default (the reference's memory_manager.py:54-74): the first decode's table is one block
+    short and the step raises IndexError, as the reference worker does at attention.py:182.
+    ``fixed_allocator=True``: 20 greedy steps whose tokens equal the oracle's (which always
+    allocates the slot it writes)."""
+    from pythonintern_b200.scheduler import ClusterMemoryManager
+    cfg = workloads.tiny_config()
+    full = workloads.reference_init_state_dict(cfg, 0)
+    prompt = workloads.tiny_prompts(1)[0][:16]
+
+    class Seq:
+        seq_id = "s"
+        prompt_token_ids = prompt
+        output_token_ids = []
+
+        @property
+        def total_length(self):
+            return len(self.prompt_token_ids) + len(self.output_token_ids)
+
+    for fixed in (False, True):
+        eng = WorkerExecutionEngine(cfg, ShardConfig(0, 1), KVCacheConfig(16, 64, str(DEV)), None, DEV)
+        eng.model.load_state_dict({k: v.to(DEV) for k, v in full.items()})
+        mm = ClusterMemoryManager(KVCacheConfig(16, 64, str(DEV)), fixed_allocator=fixed)
+        seq = Seq()
+        seq.output_token_ids = []
+        table = mm.allocate_prefill(seq)
+        resp = eng.execute_step(StepRequest(0, [SequenceSlot("s", True, prompt, 0, 16, list(table))]))
+        seq.output_token_ids.append(resp.sampled_tokens[0].token_id)
+        if not fixed:
+            mm.append_token_slot(seq)
+            with pytest.raises(IndexError):
+                eng.execute_step(StepRequest(1, [SequenceSlot("s", False, [], seq.output_token_ids[-1],
+                                                              seq.total_length, mm.get_block_table("s"))]))
+            continue
+        for step in range(1, 20):
+            mm.append_token_slot(seq)
+            resp = eng.execute_step(StepRequest(step, [SequenceSlot("s", False, [], seq.output_token_ids[-1],
+                                                                    seq.total_length, mm.get_block_table("s"))]))
+            seq.output_token_ids.append(resp.sampled_tokens[0].token_id)
+        ocfg = oracle.OracleConfig(cfg.vocab_size, cfg.hidden_dim, cfg.num_layers, cfg.num_heads,
+                                   cfg.num_kv_heads, cfg.intermediate_dim, cfg.max_seq_len, cfg.rms_norm_eps)
+        om = oracle.OracleModel(ocfg, [{k: v.numpy() for k, v in full.items()}],
+                                [oracle.KVPool(cfg.num_layers, 64, 16, cfg.num_kv_heads, cfg.head_dim)])
+        toks, _, _ = oracle.run_greedy(om, [prompt], 20, 64)
+        assert seq.output_token_ids == toks[:, 0].tolist()
