@@ -98,7 +98,7 @@ int b2_linear_swiglu(const void* x, int64_t ldx, int M, int K, const void* w_gat
                      int N, void* y, int64_t ldy, int dtype, void* workspace,
                      size_t workspace_bytes, int32_t* status, b2_stream_t stream);
 
-/* Deferred RMSNorm at world size 1 (bf16, M <= 128 rows).  Together these replace
+/* Deferred RMSNorm at world size 1 (bf16, M <= 512 rows).  Together these replace
  * RowParallelLinear.forward + the residual add + the next RMSNorm (layers.py:147-162,
  * 179-184; llama.py:70-75) followed by the next ColumnParallelLinear / SwiGLU
  * (attention.py:156-158, mlp.py:80-82), without a separate normalisation kernel:
@@ -123,7 +123,7 @@ int b2_linear_swiglu_rownorm(const void* x, int64_t ldx, int M, int K, const voi
 /* q|k|v GEMM with RoPE and the paged KV write in its epilogue: b2_linear_qkv (or, with ss
  * set, b2_linear_qkv_rownorm) followed by b2_rope_kv_write, without the intermediate
  * [M, (nq + 2 nkv) * 128] buffer (attention.py:156-158 then :46-63, :166-184).  The
- * outputs are bit-identical to the two calls.  head_dim must be 128 and M <= 128; returns
+ * outputs are bit-identical to the two calls.  head_dim must be 128 and M <= 512; returns
  * B2_ENOTSUP, before launching anything, otherwise or when the shape gets no split-K
  * cluster plan (the caller then makes the two calls).  bf16 only. */
 int b2_linear_qkv_rope_kv(const void* x, int64_t ldx, int M, int K, const void* wq, const void* wk, const void* wv,

@@ -81,8 +81,8 @@ int b2_linear_residual_norm(const void* x, int64_t ldx, int M, int K, const void
   B2_CHECK_ARG(ldx >= K && ldh >= N && ldz >= N, "b2_linear_residual_norm: row strides too small");
   if (M == 0) return B2_OK;
   B2_CHECK_ARG(w && h && norm_w && z && ss, "b2_linear_residual_norm: null pointer");
-  if (M > 128 || N % 128 != 0)
-    return b2::fail(B2_ENOTSUP, "b2_linear_residual_norm: needs M <= 128 and N %% 128 == 0 (M=%d N=%d)", M, N);
+  if (M > 512 || N % 128 != 0)
+    return b2::fail(B2_ENOTSUP, "b2_linear_residual_norm: needs M <= 512 and N %% 128 == 0 (M=%d N=%d)", M, N);
   b2::GemmSeg seg{w, N, 0};
   b2::RowNorm rn{};
   rn.res_h = h;
@@ -146,8 +146,8 @@ int b2_linear_qkv_rope_kv(const void* x, int64_t ldx, int M, int K, const void* 
   B2_CHECK_ARG(num_blocks > 0 && block_size > 0 && table_stride > 0 && layer >= 0 && max_seq_len > 0,
                "b2_linear_qkv_rope_kv: bad cache geometry");
   if (M == 0) return B2_OK;
-  if (head_dim != 128 || M > 128)
-    return b2::fail(B2_ENOTSUP, "b2_linear_qkv_rope_kv: needs head_dim 128 and at most 128 rows");
+  if (head_dim != 128 || M > 512)
+    return b2::fail(B2_ENOTSUP, "b2_linear_qkv_rope_kv: needs head_dim 128 and at most 512 rows");
   B2_CHECK_ARG(wq && wk && wv && rope_pos && block_tables && cos && sin && q_out && k_cache && v_cache,
                "b2_linear_qkv_rope_kv: null pointer");
   B2_CHECK_ARG(!ss || (n_ss > 0 && dim > 0), "b2_linear_qkv_rope_kv: bad row-norm sizes");

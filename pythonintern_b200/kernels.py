@@ -161,7 +161,8 @@ def linear_residual_norm(x: torch.Tensor, w_packed: torch.Tensor, h: torch.Tenso
 
     RowParallelLinear partial GEMM + residual add + the sums the next RMSNorm needs
     (layers.py:147-162, 179-184; llama.py:70-75).  Returns False, having launched
-    nothing, when the shape gets no split-K cluster plan (more than 128 rows).
+    nothing, when the shape gets no split-K cluster plan (too many 128-row output tiles,
+    or more than 512 rows).
     """
     require_cuda(x, "x")
     K = x.shape[-1]
@@ -217,9 +218,9 @@ def linear_qkv_rope_kv(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: 
                        layer: int, row_ss: Optional[torch.Tensor] = None, eps: float = 1e-5) -> bool:
     """``linear_qkv`` (or ``linear_qkv_rownorm`` with ``row_ss``) + ``rope_kv_write`` in one
     launch, bit-identical to the two.  Returns False, having launched nothing, when the
-    shape has no fused form (head_dim != 128, more than 128 rows, or no cluster plan)."""
+    shape has no fused form (head_dim != 128, more than 512 rows, or no cluster plan)."""
     M, K = x.shape
-    if x.dtype != torch.bfloat16 or head_dim != 128 or M > 128:
+    if x.dtype != torch.bfloat16 or head_dim != 128 or M > 512:
         return False
     _, NB, bs, ckv, chd = k_cache.shape
     assert ckv == nkv and chd == head_dim, "cache geometry does not match the heads"

@@ -168,10 +168,11 @@ class DistributedLLaMAModel(nn.Module):
         h = kernels.embedding(ids, self.embed_tokens.weight, out_dtype=torch.float32)
         xn = torch.empty(T, H, dtype=wdt, device=self.device)
         kernels.rmsnorm(h, self.layers[0].input_layernorm.weight, eps, out=xn)
-        # Deferred RMSNorm (bf16, <= 128 rows): the row-parallel GEMM adds the residual and
-        # leaves z = h * w plus per-tile sums of h^2; the next GEMM applies the row scale.
+        # Deferred RMSNorm (bf16, <= 512 rows, where the GEMM gets a split-K cluster plan):
+        # the row-parallel GEMM adds the residual and leaves z = h * w plus per-tile sums of
+        # h^2; the next GEMM applies the row scale.
         # ready: the next GEMM's input is (z, ss) rather than the normalised xn.
-        fused = wdt == torch.bfloat16 and T <= 128 and H % 128 == 0
+        fused = wdt == torch.bfloat16 and T <= 512 and H % 128 == 0
         z = torch.empty(T, H, dtype=wdt, device=self.device) if fused else None
         ss = torch.empty(T, H // 128, dtype=torch.float32, device=self.device) if fused else None
         ready = False

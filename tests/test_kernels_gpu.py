@@ -107,6 +107,7 @@ def test_linear_float32(M, N, K):
     (1, 128, 64), (1, 4096, 4096), (7, 384, 512), (16, 256, 2048), (33, 1024, 1024), (64, 512, 5632),
     (128, 6144, 4096), (129, 256, 256), (200, 384, 320), (300, 640, 2048), (1, 4096, 14336),
     (128, 14336, 4096), (100, 12800, 1024), (64, 10240, 2048),  # 74..147 tiles: one wave, idle SMs
+    (240, 768, 4096), (240, 4096, 14336), (512, 4096, 7168), (513, 512, 1024),  # 128-wide token tiles to 512
 ])
 def test_linear_bf16_tensor_cores(M, N, K):
     """tcgen05 GEMM (swap-AB, split-K where chosen) against the float64 oracle on the same bf16 inputs."""
@@ -179,7 +180,7 @@ def test_large_gemm_repeated_calls_are_identical():
     assert rel(to_np(y2), to_np(x) @ to_np(wg).T) < 8e-3
 
 
-@pytest.mark.parametrize("M", [128, 5])
+@pytest.mark.parametrize("M", [128, 5, 240])
 def test_deferred_rmsnorm_producer_and_consumers(M):
     """Row-parallel GEMM + residual add leaving z = h * w and per-tile sums of h^2, then
     q|k|v and SwiGLU GEMMs that apply the RMS scale per row: against float64 on the same
@@ -216,7 +217,8 @@ def test_deferred_rmsnorm_producer_and_consumers(M):
     assert rel(to_np(q), want) < 8e-3
 
 
-@pytest.mark.parametrize("M,nq,nkv,rownorm", [(128, 32, 8, False), (128, 4, 1, True), (7, 8, 2, True)])
+@pytest.mark.parametrize("M,nq,nkv,rownorm", [(128, 32, 8, False), (128, 4, 1, True), (7, 8, 2, True),
+                                               (240, 4, 1, True), (300, 8, 2, False)])
 def test_fused_qkv_rope_kv_is_bit_identical(M, nq, nkv, rownorm):
     """q|k|v GEMM with RoPE and the paged KV write in its epilogue equals the GEMM followed
     by rope_kv_write, bit for bit: q, and every K/V slot of the pool."""
@@ -246,6 +248,21 @@ def test_fused_qkv_rope_kv_is_bit_identical(M, nq, nkv, rownorm):
         outs.append((q, kc, vc))
     for a, b in zip(*outs):
         assert torch.equal(a, b)
+
+
+def test_fused_qkv_rope_kv_declines_shapes_without_a_cluster_plan():
+    """240 rows of the 8B TP=1 q|k|v (96 output tiles) get no split-K cluster plan: the fused
+    call launches nothing and says so, and the caller's two-call path runs instead."""
+    M, hd, K = 240, 128, 4096
+    x = torch.randn(M, K, generator=g(3)).to(DEV, torch.bfloat16)
+    wq, wk, wv = [torch.zeros(n * hd, K, dtype=torch.bfloat16, device=DEV) for n in (32, 8, 8)]
+    kc = torch.zeros(1, 64, 16, 8, hd, dtype=torch.bfloat16, device=DEV)
+    q = torch.empty(M, 32 * hd, dtype=torch.bfloat16, device=DEV)
+    tables = torch.zeros(M, 1, dtype=torch.int32, device=DEV)
+    pos = torch.zeros(M, dtype=torch.int64, device=DEV)
+    tab = torch.zeros(16, hd, device=DEV)
+    assert not kernels.linear_qkv_rope_kv(x, wq, wk, wv, 32, 8, hd, pos, None, None, tables, tab, tab, q, kc,
+                                          kc.clone(), 0)
 
 
 def test_split_k_workspace_shared_across_shapes():
