@@ -79,7 +79,7 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the TP parity leg (it runs before timing)")
     ap.add_argument("--no-sweep", action="store_true", help="skip the row-parallel sweep at TP > 1")
-    ap.add_argument("--workload", choices=["decode", "prefill", "allreduce"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "allreduce", "mixed"], default="decode")
     ap.add_argument("--prompts", type=int, default=16, help="prefill workload: prompts per step")
     ap.add_argument("--prompt-len", type=int, default=1024, help="prefill workload: tokens per prompt")
     return ap.parse_args(argv)
@@ -1168,6 +1168,204 @@ def run_prefill(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- mixed continuous-batching step
+MIXED_PREFILLS, MIXED_PROMPT, MIXED_DECODES, MIXED_CTX = 16, 1024, 240, (512, 8192)
+
+
+def mixed_layout(seed: int):
+    """One mixed step's sequences: 16 prompts of 1024 tokens and 240 decodes whose contexts are
+    uniform in [512, 8192] (seeded); every sequence's blocks from one seeded permutation."""
+    rng = np.random.default_rng(seed + 11)
+    dec_ctx = rng.integers(MIXED_CTX[0], MIXED_CTX[1] + 1, size=MIXED_DECODES).astype(np.int64)
+    nblk_p = math.ceil(MIXED_PROMPT / 16)
+    nblk_d = [math.ceil(int(c) / 16) for c in dec_ctx]
+    total = MIXED_PREFILLS * nblk_p + sum(nblk_d) + 8
+    perm = rng.permutation(total).astype(np.int64)
+    k, tp, td = 0, [], []
+    for _ in range(MIXED_PREFILLS):
+        tp.append(perm[k:k + nblk_p].tolist())
+        k += nblk_p
+    for n in nblk_d:
+        td.append(perm[k:k + n].tolist())
+        k += n
+    prompts = rng.integers(0, 32000, size=(MIXED_PREFILLS, MIXED_PROMPT)).astype(np.int64)
+    dec_tok = rng.integers(0, 32000, size=MIXED_DECODES).astype(np.int64)
+    return prompts, tp, dec_ctx, dec_tok, td, total
+
+
+def run_mixed(args):
+    """Config 4: one continuous-batching step of the Mistral-7B shape (vocab 32000) holding 16
+    prefills of 1024 tokens and 240 decodes at contexts uniform in [512, 8192], tensor parallel
+    over the ranks.  The reference runs the prefills one forward each and then the decodes as
+    one batch (engine/worker/execution_engine.py:85-145); here the step is one varlen prefill
+    forward plus one replay of the captured decode step.  Metric: tokens processed per second
+    (prompt tokens + decode tokens) by the step."""
+    import torch
+    import torch.distributed as dist
+
+    from pythonintern_b200 import _lib, workloads
+    from pythonintern_b200.config import KVCacheConfig, ShardConfig
+    from pythonintern_b200.model.metadata import build_prefill_metadata
+    from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
+    from pythonintern_b200.worker.execution_engine import WorkerExecutionEngine
+    from pythonintern_b200.worker.graphs import DecodeGraph, table_bucket
+    from pythonintern_b200.worker.messages import SequenceSlot, StepRequest
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=180), device_id=dev)
+    cfg = workloads.mistral_7b_config(num_layers=args.layers, max_seq_len=8448)
+    W, K = args.warmup, args.steps
+    prompts, tp, dec_ctx, dec_tok, td, num_blocks = mixed_layout(args.seed)
+    T_p = MIXED_PREFILLS * MIXED_PROMPT
+    comm = None
+    if world > 1:
+        comm = DistributedCommunicator(rank, world, device=dev, max_bytes=T_p * cfg.hidden_dim * 2)
+        comm.connect()
+    engine = WorkerExecutionEngine(cfg, ShardConfig(rank=rank, world_size=world),
+                                   KVCacheConfig(block_size=16, num_blocks=num_blocks, device=str(dev)), comm, dev,
+                                   max_prefill_tokens=T_p)
+    model, pool = engine.model, engine.kv_manager.pool
+    init_synthetic(model, pool, args.seed, rank, dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------- device-timed: the step's inputs resident in HBM
+    md_p = build_prefill_metadata([MIXED_PROMPT] * MIXED_PREFILLS, tp, dev)
+    ids_p = torch.from_numpy(prompts.reshape(1, T_p)).to(dev)
+    graph = DecodeGraph(model, pool, MIXED_DECODES, table_bucket(max(len(t) for t in td)))
+    graph.meta.copy_(torch.from_numpy(graph.pack(dec_tok, dec_ctx - 1, td, np.zeros(graph.nbytes, np.uint8))).to(dev))
+    c0 = _lib.launch_count
+    graph.capture()
+    dec_launches = (_lib.launch_count - c0) // 2
+
+    def prefill(i):
+        return model.greedy(ids_p, None, pool, tp, True, i, metadata=md_p)
+
+    def step(i):
+        prefill(i)
+        return graph.replay()
+
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize(dev)
+    _lib.check_device_status(dev, "mixed warm-up")
+    barrier()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    c1 = _lib.launch_count
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(W, W + K):
+        step(i)
+    ev1.record(stream)
+    ev1.synchronize()
+    clk = clocks.stop()
+    launches = (_lib.launch_count - c1) + dec_launches * K
+    barrier()
+    torch.cuda.synchronize(dev)
+    _lib.check_device_status(dev, "timed mixed step")
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    tokens = T_p + MIXED_DECODES
+    value = tokens * K / (ms / 1000.0)
+
+    # ---------------- the two halves timed apart (same inputs)
+    def time_part(fn, reps=3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for r in range(reps):
+            fn(r)
+        e1.record(stream)
+        e1.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / reps)
+    ms_pre = time_part(prefill)
+    ms_dec = time_part(lambda r: graph.replay())
+    g_fl, a_fl = prefill_flops(cfg, [MIXED_PROMPT] * MIXED_PREFILLS, world)
+    H, hd, nkv, L = cfg.hidden_dim, cfg.head_dim, cfg.num_kv_heads, cfg.num_layers
+    wbytes = L * (H * (cfg.num_heads + 2 * nkv) * hd + cfg.num_heads * hd * H + 3 * H * cfg.intermediate_dim) * 2
+    kv_bytes = L * int(dec_ctx.sum()) * 2 * nkv * hd * 2
+    dec_bytes = (wbytes + kv_bytes) / world + cfg.vocab_size * H * 2 / world
+    t_peak, t_kind = measured_tensor_peak()
+    h_peak, h_kind = measured_peaks()
+    pre_tf = (g_fl + a_fl) / (ms_pre / 1000.0) / 1e12
+    dec_gbs = dec_bytes / (ms_dec / 1000.0) / 1e9
+    roofline = {"bound": "tensor", "kernel": "prefill half of the step (all its GEMMs and attention)",
+                "achieved": pre_tf, "peak": t_peak, "unit": "TFLOP/s", "frac": pre_tf / t_peak,
+                "peak_source": f"{t_kind} (bf16_tflops)", "traffic": None,
+                "share_of_step": ms_pre / (ms / K),
+                "decode_half": {"ms": ms_dec, "algorithmic_bytes": dec_bytes, "gbs": dec_gbs, "peak_gbs": h_peak,
+                                "frac": dec_gbs / h_peak, "peak_source": f"{h_kind} (hbm_gbs)"}}
+
+    # ---------------- end to end through execute_step: host prompts, tables and tokens
+    e2e = None
+    if not args.no_e2e:
+        h2d = d2h = 0
+
+        def e2e_step(i):
+            slots = [SequenceSlot(seq_id=f"p{s}", is_prefill=True, prompt_token_ids=prompts[s].tolist(),
+                                  current_len=MIXED_PROMPT, block_table=tp[s]) for s in range(MIXED_PREFILLS)]
+            slots += [SequenceSlot(seq_id=f"d{d}", is_prefill=False, current_token_id=int(dec_tok[d]),
+                                   current_len=int(dec_ctx[d]), block_table=td[d]) for d in range(MIXED_DECODES)]
+            engine.execute_step(StepRequest(step_id=i, active_sequences=slots))
+
+        for i in range(W):
+            e2e_step(i)
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(W, W + K):
+            e2e_step(i)
+            h2d, d2h = engine.last_h2d_bytes, engine.last_d2h_bytes
+        e1.record(stream)
+        e1.synchronize()
+        ms_e2e = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": tokens * K / (ms_e2e / 1000.0), "unit": "tokens/s", "ms_per_step": ms_e2e / K,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "api": "WorkerExecutionEngine.execute_step(StepRequest) with 16 prefill + 240 decode slots"}
+
+    if rank == 0:
+        line = {
+            "metric": "mixed-step tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: N(0,0.02) weights, random KV cache and prompts, random block-table permutation",
+            "config": {"workload": (f"mistral-7b-shape mixed step: {MIXED_PREFILLS} prefills x {MIXED_PROMPT} tokens "
+                                    f"+ {MIXED_DECODES} decodes at contexts uniform {MIXED_CTX[0]}-{MIXED_CTX[1]}, "
+                                    f"TP={world} ({cfg.num_layers} layers)"),
+                       "model": "mistral-7b-shape", "global_batch": MIXED_PREFILLS + MIXED_DECODES,
+                       "seq_len": MIXED_PROMPT, "parallelism": f"tp{world}",
+                       "l2": "inputs larger than L2 (weights + KV read per step >> 126 MB)"},
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": None, "clocks": clk, "gpu_launches": launches,
+            "parts_ms": {"prefill": ms_pre, "decode": ms_dec},
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if comm is not None:
+        barrier()
+        comm.cleanup()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 # ----------------------------------------------------------------------------- row-parallel all-reduce
 def run_allreduce(args):
     import torch
@@ -1215,6 +1413,8 @@ def main(argv=None):
         return run_prefill(args)
     if args.workload == "allreduce":
         return run_allreduce(args)
+    if args.workload == "mixed":
+        return run_mixed(args)
     return run_ours(args)
 
 

@@ -418,3 +418,57 @@ def test_fixed_allocator_mode_end_to_end():
                                 [oracle.KVPool(cfg.num_layers, 64, 16, cfg.num_kv_heads, cfg.head_dim)])
         toks, _, _ = oracle.run_greedy(om, [prompt], 20, 64)
         assert seq.output_token_ids == toks[:, 0].tolist()
+
+
+def test_mixed_step_mistral_shape_against_oracle():
+    """A continuous-batching step that mixes prefills and decodes (the Mistral-7B shape of the
+    mixed-step benchmark, 2 layers, vocab 4096): step 0 prefills five sequences; step 1 holds
+    three new prefills and the five sequences' first decodes, at contexts 100-300.  The engine
+    batches the step's prompts into one varlen forward and replays a captured decode step; the
+    oracle runs the reference's order (one forward per prompt, then the decodes as one batch,
+    execution_engine.py:85-145).  Top logits within the bf16 tolerance, greedy tokens equal
+    wherever the oracle's margin clears the bf16 error bound."""
+    cfg = workloads.mistral_7b_config(num_layers=2, max_seq_len=1024)
+    cfg.vocab_size = 4096
+    sd = workloads.synthetic_state_dict(cfg, seed=41)
+    eng = WorkerExecutionEngine(cfg, ShardConfig(0, 1), KVCacheConfig(16, 128, str(DEV)), None, DEV)
+    eng.model.load_state_dict(sd)
+    ocfg = oracle.OracleConfig(cfg.vocab_size, cfg.hidden_dim, cfg.num_layers, cfg.num_heads, cfg.num_kv_heads,
+                               cfg.intermediate_dim, cfg.max_seq_len, cfg.rms_norm_eps)
+    om = oracle.OracleModel(ocfg, [{k: v.float().numpy() for k, v in sd.items()}],
+                            [oracle.KVPool(cfg.num_layers, 128, 16, cfg.num_kv_heads, cfg.head_dim)])
+    gen = torch.Generator().manual_seed(42)
+    dec_lens = [299, 100, 180, 257, 133]
+    new_lens = [64, 17, 96]
+    perm = torch.randperm(128, generator=gen).tolist()
+    tables, k = [], 0
+    for n in dec_lens + new_lens:
+        nb = math.ceil((n + 1) / 16)
+        tables.append(perm[k:k + nb])
+        k += nb
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=gen).tolist() for n in dec_lens + new_lens]
+    nd = len(dec_lens)
+    s0 = [SequenceSlot(f"d{i}", True, prompts[i], 0, dec_lens[i], tables[i]) for i in range(nd)]
+    o0 = [oracle.Slot(f"d{i}", True, prompts[i], 0, dec_lens[i], tables[i]) for i in range(nd)]
+    eng.execute_step(StepRequest(0, s0))
+    ref0 = oracle.execute_step(om, o0)
+    toks = [t for _, t, _ in ref0]
+    s1 = [SequenceSlot(f"n{j}", True, prompts[nd + j], 0, new_lens[j], tables[nd + j]) for j in range(len(new_lens))]
+    s1 += [SequenceSlot(f"d{i}", False, [], toks[i], dec_lens[i] + 1, tables[i]) for i in range(nd)]
+    o1 = [oracle.Slot(s.seq_id, s.is_prefill, s.prompt_token_ids, s.current_token_id, s.current_len, s.block_table)
+          for s in s1]
+    resp = eng.execute_step(StepRequest(1, s1))
+    ref1 = oracle.execute_step(om, o1)
+    _lib.check_device_status(DEV, "mixed step")
+    assert [t.seq_id for t in resp.sampled_tokens] == [sid for sid, _, _ in ref1]
+    got = np.asarray([t.top_logits for t in resp.sampled_tokens])
+    want = np.asarray([tl for _, _, tl in ref1])
+    err = float(np.abs(got - want).max())
+    assert rel(got, want) < 2e-2 and err < 0.15, (rel(got, want), err)
+    srt = np.sort(om.last_logits, axis=-1)
+    margin = srt[:, -1] - srt[:, -2]
+    sel = margin > max(0.05, 3 * err)
+    assert sel.sum() >= 4
+    g = np.asarray([t.token_id for t in resp.sampled_tokens])
+    w = np.asarray([t for _, t, _ in ref1])
+    assert np.array_equal(g[sel], w[sel])
