@@ -318,8 +318,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_attn_simt_kernel(AttnPa
 //
 // A CTA owns one (row, kv head, split); each of its 4 warps walks every 4th KV block
 // of the CTA's run with its own STAGES-deep cp.async ring of whole blocks (16 token
-// rows of K and of V for this kv head): 3 stages with two CTAs per SM, 6 stages when the
-// grid has at most one CTA per SM, so 8-10 blocks per SM are in flight either way.  Rows are
+// rows of K and of V for this kv head), so 12 blocks per CTA are in flight.  Rows are
 // stored in shared memory with their 16-byte chunks XOR-swizzled by (row & 7), which
 // keeps the ldmatrix reads below free of bank conflicts.  Per block a warp computes
 //   S[16 x 16]  = Q[16 x HD] . K^T   (the REP <= 8 query heads of the group are rows
@@ -328,8 +327,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_attn_simt_kernel(AttnPa
 // with an online softmax in the log2 domain.  The float32 softmax statistics, the
 // per-warp merge and the split merge are shared with the SIMT kernel.
 constexpr int kMmaWarps = 4;
-constexpr int kMmaStages = 3;      // two CTAs per SM: enough warps in flight once the grid fills the GPU
-constexpr int kMmaDeepStages = 6;  // one CTA per SM: a grid of at most one CTA per SM keeps 5 blocks in flight per warp
+constexpr int kMmaStages = 3;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -370,7 +368,6 @@ struct MmaCfg {
   static constexpr int BLKB = 16 * ROWB;      // one K (or V) block
   static constexpr int STAGEB = 2 * BLKB;     // K + V
   static constexpr size_t SMEM = (size_t)kMmaWarps * kMmaStages * STAGEB;
-  static constexpr size_t smem(int stages) { return (size_t)kMmaWarps * stages * STAGEB; }
 };
 
 template <int HD>
@@ -378,9 +375,8 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return (uint32_t)(row * MmaCfg<HD>::ROWB + ((chunk ^ (row & MmaCfg<HD>::SWZ)) << 4));
 }
 
-template <int HD, int REP, int STAGES>
-__global__ void __launch_bounds__(kMmaWarps * 32, STAGES <= kMmaStages ? 2 : 1)
-    paged_attn_mma_kernel(AttnParams p) {
+template <int HD, int REP>
+__global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnParams p) {
   pdl_wait();
   pdl_trigger();
   using C = MmaCfg<HD>;
@@ -418,14 +414,14 @@ __global__ void __launch_bounds__(kMmaWarps * 32, STAGES <= kMmaStages ? 2 : 1)
   const int64_t tok_stride_b = (int64_t)p.nkv * HD * 2;  // bytes between token rows of the pool
   const char* kbase = reinterpret_cast<const char*>(p.k_cache) + (p.layer_off + (int64_t)g * HD) * 2;
   const char* vbase = reinterpret_cast<const char*>(p.v_cache) + (p.layer_off + (int64_t)g * HD) * 2;
-  const uint32_t wsm = smem_addr(smem) + (uint32_t)(warp * STAGES * C::STAGEB);
+  const uint32_t wsm = smem_addr(smem) + (uint32_t)(warp * kMmaStages * C::STAGEB);
 
   // Issue the copies of this warp's i-th block into ring slot (i % STAGES); a block id
   // outside the pool is not copied, and the main loop skips that block.
   auto issue = [&](int i) {
     const int blk = table[blk0 + warp + i * kMmaWarps];
     if (blk < 0 || blk >= p.num_blocks) return;
-    const uint32_t st = wsm + (uint32_t)((i % STAGES) * C::STAGEB);
+    const uint32_t st = wsm + (uint32_t)((i % kMmaStages) * C::STAGEB);
     const int64_t blk_off = (int64_t)blk * bs * tok_stride_b;
 #pragma unroll
     for (int q = lane; q < 16 * C::CHUNKS; q += 32) {
@@ -442,14 +438,14 @@ __global__ void __launch_bounds__(kMmaWarps * 32, STAGES <= kMmaStages ? 2 : 1)
   float m_run = -INFINITY, l_run = 0.f;  // row qr statistics (per-lane partial l)
 
 #pragma unroll
-  for (int i = 0; i < STAGES - 1; ++i) {
+  for (int i = 0; i < kMmaStages - 1; ++i) {
     if (i < n_w) issue(i);
     cp_async_commit();
   }
   for (int i = 0; i < n_w; ++i) {
-    if (i + STAGES - 1 < n_w) issue(i + STAGES - 1);
+    if (i + kMmaStages - 1 < n_w) issue(i + kMmaStages - 1);
     cp_async_commit();
-    cp_async_wait<STAGES - 1>();
+    cp_async_wait<kMmaStages - 1>();
     __syncwarp();
     const int bidx = blk0 + warp + i * kMmaWarps;
     const int blk = table[bidx];
@@ -461,7 +457,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, STAGES <= kMmaStages ? 2 : 1)
       __syncwarp();
       continue;
     }
-    const uint32_t ks = wsm + (uint32_t)((i % STAGES) * C::STAGEB);
+    const uint32_t ks = wsm + (uint32_t)((i % kMmaStages) * C::STAGEB);
     const uint32_t vs = ks + C::BLKB;
 
     // S = Q K^T over 16 tokens: two 8-token n-tiles.
@@ -820,33 +816,22 @@ static int allow_dynamic_smem(const void* fn, size_t bytes) {
   return B2_OK;
 }
 
-template <int HD, int STAGES>
-static int launch_mma_rep_st(int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {
-  const size_t smem = MmaCfg<HD>::smem(STAGES);
+template <int HD>
+static int launch_mma_rep(int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {
+  using C = MmaCfg<HD>;
   auto go = [&](void (*k)(AttnParams)) -> int {
-    const int rc = allow_dynamic_smem((const void*)k, smem);
+    const int rc = allow_dynamic_smem((const void*)k, C::SMEM);
     if (rc) return rc;
-    B2_TRY_CUDA(launch_pdl(k, grid, dim3(kMmaWarps * 32), smem, s, p));
+    B2_TRY_CUDA(launch_pdl(k, grid, dim3(kMmaWarps * 32), C::SMEM, s, p));
     return B2_OK;
   };
   switch (rep) {
-    case 1: return go(paged_attn_mma_kernel<HD, 1, STAGES>);
-    case 2: return go(paged_attn_mma_kernel<HD, 2, STAGES>);
-    case 4: return go(paged_attn_mma_kernel<HD, 4, STAGES>);
-    case 8: return go(paged_attn_mma_kernel<HD, 8, STAGES>);
+    case 1: return go(paged_attn_mma_kernel<HD, 1>);
+    case 2: return go(paged_attn_mma_kernel<HD, 2>);
+    case 4: return go(paged_attn_mma_kernel<HD, 4>);
+    case 8: return go(paged_attn_mma_kernel<HD, 8>);
     default: return fail(B2_ENOTSUP, "b2_paged_attention: nq/nkv = %d not supported (1, 2, 4, 8)", rep);
   }
-}
-
-// A grid that fills at most one CTA per SM (few (row, kv head, split) triples: tensor
-// parallelism over 8 GPUs leaves one kv head per rank) gets the deep ring: its 4 warps
-// per SM must keep as many bytes in flight as 8 warps of the two-CTA configuration.  The
-// pipeline depth changes no arithmetic, so both configurations give identical results.
-template <int HD>
-static int launch_mma_rep(int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {
-  const long ctas = (long)grid.x * grid.y * grid.z;
-  if (ctas <= sm_count()) return launch_mma_rep_st<HD, kMmaDeepStages>(rep, p, grid, s);
-  return launch_mma_rep_st<HD, kMmaStages>(rep, p, grid, s);
 }
 
 static int launch_mma(int hd, int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {

@@ -256,9 +256,7 @@ def rope_kv_write(qkv: torch.Tensor, nq: int, nkv: int, head_dim: int, rope_pos:
 
 def attention_splits(n_rows: int, nkv: int, max_ctx: int, block_size: int = 16, device=None) -> int:
     """KV split count: as many splits as keep every (row, kv head, split) CTA in ONE wave
-    (two attention CTAs are resident per SM), with at least 4 KV blocks per split; when
-    fewer (row, kv head) pairs than SMs exist, at most one CTA per SM (the kernel's deep
-    ring) with at least 8 blocks per split.
+    (two attention CTAs are resident per SM), with at least 4 KV blocks per split.
 
     A second, partly filled wave leaves HBM idle at the tail (measured on B200 at context
     2048, batch 128: one kv head per row, 5 splits over 2.2 waves took 40 us, 2 splits in
@@ -273,10 +271,6 @@ def attention_splits(n_rows: int, nkv: int, max_ctx: int, block_size: int = 16, 
     if pairs >= slots:
         return 1
     nblk = 32 * max(1, math.ceil(max_ctx / (32 * block_size)))
-    if pairs < sms:
-        # at most one CTA per SM: the kernel switches to its deep (6-stage) ring, whose
-        # 4 warps keep as much in flight as two 3-stage CTAs; 8+ blocks per split
-        return max(1, min(sms // pairs, max(1, nblk // 8), 256))
     s = min(slots // pairs, max(1, nblk // 4), 256)
     return max(1, s)
 
