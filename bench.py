@@ -79,7 +79,7 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the TP parity leg (it runs before timing)")
     ap.add_argument("--no-sweep", action="store_true", help="skip the row-parallel sweep at TP > 1")
-    ap.add_argument("--workload", choices=["decode", "prefill", "allreduce", "mixed"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "allreduce", "mixed", "tinyllama"], default="decode")
     ap.add_argument("--prompts", type=int, default=16, help="prefill workload: prompts per step")
     ap.add_argument("--prompt-len", type=int, default=1024, help="prefill workload: tokens per prompt")
     return ap.parse_args(argv)
@@ -1366,6 +1366,207 @@ def run_mixed(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- continuous batching, TinyLlama
+TL_REQUESTS, TL_PROMPT, TL_NEW = 64, (128, 512), 128
+
+
+def tinyllama_job(seed: int):
+    """64 requests with prompts uniform in [128, 512] tokens (seeded), 128 new tokens each; block
+    tables cover prompt + new tokens, all slices of one seeded permutation of the pool."""
+    rng = np.random.default_rng(seed + 23)
+    lens = rng.integers(TL_PROMPT[0], TL_PROMPT[1] + 1, size=TL_REQUESTS).astype(np.int64)
+    prompts = [rng.integers(0, 32000, size=int(n)).astype(np.int64) for n in lens]
+    nblk = [math.ceil((int(n) + TL_NEW) / 16) for n in lens]
+    total = sum(nblk) + 8
+    perm = rng.permutation(total).astype(np.int64)
+    tables, k = [], 0
+    for n in nblk:
+        tables.append(perm[k:k + n].tolist())
+        k += n
+    return prompts, lens, tables, total
+
+
+def run_tinyllama(args):
+    """Config 2: TinyLlama 1.1B shape (bf16), 64 requests admitted together (continuous batching
+    with max_batch_size >= 64, so the batcher's first step prefills them all and every later
+    step decodes all 64, engine/scheduler/continuous_batcher.py:53-108), 128 greedy tokens each,
+    tensor parallel over the ranks.  One bench step = the whole job (1 prefill step + 127
+    decode steps); metric = generated tokens per second."""
+    import torch
+    import torch.distributed as dist
+
+    from pythonintern_b200 import _lib, workloads
+    from pythonintern_b200.config import KVCacheConfig, ShardConfig
+    from pythonintern_b200.model.metadata import build_prefill_metadata
+    from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
+    from pythonintern_b200.worker.execution_engine import WorkerExecutionEngine
+    from pythonintern_b200.worker.graphs import DecodeGraph, table_bucket
+    from pythonintern_b200.worker.messages import SequenceSlot, StepRequest
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=180), device_id=dev)
+    cfg = workloads.tinyllama_config(num_layers=22 if args.layers == 32 else args.layers)
+    cfg.max_seq_len = 1024
+    W, K = args.warmup, args.steps
+    prompts, lens, tables, num_blocks = tinyllama_job(args.seed)
+    T_p = int(lens.sum())
+    comm = None
+    if world > 1:
+        comm = DistributedCommunicator(rank, world, device=dev, max_bytes=T_p * cfg.hidden_dim * 2)
+        comm.connect()
+    engine = WorkerExecutionEngine(cfg, ShardConfig(rank=rank, world_size=world),
+                                   KVCacheConfig(block_size=16, num_blocks=num_blocks, device=str(dev)), comm, dev,
+                                   max_prefill_tokens=T_p)
+    model, pool = engine.model, engine.kv_manager.pool
+    init_synthetic(model, pool, args.seed, rank, dev)
+    stream = torch.cuda.current_stream(dev)
+    B = TL_REQUESTS
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------- device-timed job: prompts, tables and every decode step's metadata resident
+    md_p = build_prefill_metadata(lens.tolist(), tables, dev)
+    ids_p = torch.from_numpy(np.concatenate(prompts)[None]).to(dev)
+    graph = DecodeGraph(model, pool, B, table_bucket(max(len(t) for t in tables)))
+    packed = []
+    for i in range(1, TL_NEW):
+        buf = graph.pack(np.zeros(B, np.int64), lens - 1 + i, tables, np.zeros(graph.nbytes, np.uint8))
+        packed.append(torch.from_numpy(buf).to(dev))
+    graph.meta.copy_(packed[0])
+    c0 = _lib.launch_count
+    graph.capture()
+    dec_launches = (_lib.launch_count - c0) // 2
+    out_tok = torch.empty(TL_NEW, B, dtype=torch.int64, device=dev)
+
+    def job():
+        tok, _ = model.greedy(ids_p, None, pool, tables, True, 0, metadata=md_p)
+        out_tok[0].copy_(tok.view(-1))
+        for i in range(1, TL_NEW):
+            graph.meta.copy_(packed[i - 1])
+            graph.tok.copy_(out_tok[i - 1].view(B, 1))
+            nt, _ = graph.replay()
+            out_tok[i].copy_(nt.view(-1))
+
+    for _ in range(W):
+        job()
+    torch.cuda.synchronize(dev)
+    _lib.check_device_status(dev, "tinyllama warm-up")
+    barrier()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    c1 = _lib.launch_count
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(K):
+        job()
+    ev1.record(stream)
+    ev1.synchronize()
+    clk = clocks.stop()
+    launches = (_lib.launch_count - c1) + dec_launches * (TL_NEW - 1) * K
+    barrier()
+    torch.cuda.synchronize(dev)
+    _lib.check_device_status(dev, "timed tinyllama job")
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    gen = B * TL_NEW
+    value = gen * K / (ms / 1000.0)
+
+    # decode steps alone: HBM roofline of the decode step (weights + KV read per step)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for i in range(1, TL_NEW):
+        graph.meta.copy_(packed[i - 1])
+        graph.replay()
+    e1.record(stream)
+    e1.synchronize()
+    ms_dec = max_over_ranks(e0.elapsed_time(e1)) / (TL_NEW - 1)
+    H, hd, nkv, L = cfg.hidden_dim, cfg.head_dim, cfg.num_kv_heads, cfg.num_layers
+    wbytes = L * (H * (cfg.num_heads + 2 * nkv) * hd + cfg.num_heads * hd * H + 3 * H * cfg.intermediate_dim) * 2
+    kv_avg = float(lens.mean()) + TL_NEW / 2
+    dec_bytes = (wbytes + L * B * kv_avg * 2 * nkv * hd * 2) / world + cfg.vocab_size * H * 2 / world
+    peak, kind = measured_peaks()
+    gbs = dec_bytes / (ms_dec / 1000.0) / 1e9
+    roofline = {"bound": "hbm", "kernel": "decode step (captured graph), weights + KV per step", "achieved": gbs,
+                "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_source": f"{kind} (hbm_gbs)", "traffic": None,
+                "algorithmic_bytes_per_step": dec_bytes, "decode_step_ms": ms_dec,
+                "share_of_job": ms_dec * (TL_NEW - 1) / (ms / K)}
+
+    # ---------------- end to end: the job through execute_step with a host-side batcher
+    e2e = None
+    if not args.no_e2e:
+        h2d = d2h = 0
+
+        def e2e_job():
+            nonlocal h2d, d2h
+            slots = [SequenceSlot(seq_id=f"r{r}", is_prefill=True, prompt_token_ids=prompts[r].tolist(),
+                                  current_len=int(lens[r]), block_table=tables[r]) for r in range(B)]
+            resp = engine.execute_step(StepRequest(step_id=0, active_sequences=slots))
+            h2d, d2h = engine.last_h2d_bytes, engine.last_d2h_bytes
+            cur = {t.seq_id: t.token_id for t in resp.sampled_tokens}
+            for i in range(1, TL_NEW):
+                slots = [SequenceSlot(seq_id=f"r{r}", is_prefill=False, current_token_id=cur[f"r{r}"],
+                                      current_len=int(lens[r]) + i, block_table=tables[r]) for r in range(B)]
+                resp = engine.execute_step(StepRequest(step_id=i, active_sequences=slots))
+                cur = {t.seq_id: t.token_id for t in resp.sampled_tokens}
+                h2d += engine.last_h2d_bytes
+                d2h += engine.last_d2h_bytes
+
+        for _ in range(W):
+            e2e_job()
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(K):
+            e2e_job()
+        e1.record(stream)
+        e1.synchronize()
+        ms_e2e = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": gen * K / (ms_e2e / 1000.0), "unit": "tokens/s", "ms_per_step": ms_e2e / K,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "api": "WorkerExecutionEngine.execute_step: 1 prefill step of 64 prompts + 127 decode steps"}
+
+    if rank == 0:
+        line = {
+            "metric": "generated tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: N(0,0.02) weights, random prompts, random block-table permutation",
+            "config": {"workload": (f"tinyllama-1.1b-shape continuous batching: {B} requests, prompts uniform "
+                                    f"{TL_PROMPT[0]}-{TL_PROMPT[1]} tokens, {TL_NEW} greedy tokens each, one step = "
+                                    f"the whole job, TP={world} ({cfg.num_layers} layers)"),
+                       "model": "tinyllama-1.1b-shape", "global_batch": B, "seq_len": TL_PROMPT[1] + TL_NEW,
+                       "parallelism": f"tp{world}",
+                       "l2": "inputs larger than L2 (2.2 GB of weights read per decode step)"},
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": None, "clocks": clk, "gpu_launches": launches,
+            "prompt_tokens_per_job": T_p,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if comm is not None:
+        barrier()
+        comm.cleanup()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 # ----------------------------------------------------------------------------- row-parallel all-reduce
 def run_allreduce(args):
     import torch
@@ -1415,6 +1616,8 @@ def main(argv=None):
         return run_allreduce(args)
     if args.workload == "mixed":
         return run_mixed(args)
+    if args.workload == "tinyllama":
+        return run_tinyllama(args)
     return run_ours(args)
 
 

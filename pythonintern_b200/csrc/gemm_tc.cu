@@ -1022,16 +1022,23 @@ static int max_active_clusters(int BN, bool swiglu, int s) {
 // than 128 (BN = 256).
 static Plan make_plan(int M, int n_tiles, int K, bool swiglu) {
   Plan pl{};
-  // Up to 512 tokens the token tiles stay 128 wide (2-4 of them): the weight tiles are then
-  // read once per token tile from L2, but every tile's mainloop streams its full K without
-  // the 256-wide tile's slow single-CTA split-K reduction (measured on B200 at 240 decode
-  // rows: q|k|v 58 us with 256-wide tiles).  Above 512 tokens 256-wide tiles halve the
-  // weight re-reads, which is what the prefill GEMMs need.
-  pl.BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 512 ? 128 : 256;
+  // 129-512 tokens: 256-wide token tiles when they alone give the persistent kernel at
+  // least half a wave (no split-K); otherwise 128-wide tiles, which keep the split-K
+  // cluster path and the fused epilogues instead of the 256-wide tile's single-CTA
+  // split-K reduction (measured on B200 at 240 decode rows, 8B shape: q|k|v 58 -> 32 us,
+  // o_proj 52 -> 17 us at TP=1; gate|up, 112 weight tiles, stays at 256: 76 vs 85 us).
+  const int sms = sm_count();
+  if (M <= 128) {
+    pl.BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  } else if (M <= 512) {
+    const long t256 = (long)n_tiles * ((M + 255) / 256);
+    pl.BN = 2 * t256 >= sms ? 256 : 128;
+  } else {
+    pl.BN = 256;
+  }
   pl.m_tiles = (M + pl.BN - 1) / pl.BN;
   pl.n_tiles = n_tiles;
   pl.nkb = (K + BK - 1) / BK;
-  const int sms = sm_count();
   const long tiles = (long)n_tiles * pl.m_tiles;
   pl.splits = 1;
   pl.kbps = pl.nkb;
