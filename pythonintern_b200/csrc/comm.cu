@@ -780,11 +780,40 @@ int b2_allreduce_rmsnorm_sharded(b2_comm* comm, int rows, int dim, int dtype, fl
   B2_CHECK_ARG(((uintptr_t)h_slice % 16) == 0 && ((uintptr_t)norm_w % 16) == 0 && ((uintptr_t)y % 16) == 0,
                "b2_allreduce_rmsnorm_sharded: h_slice, norm_w and y must be 16-byte aligned");
   const b2::CommView v = b2::make_view(comm);
-  int grid = R < 64 ? 64 : R;
-  if (grid > b2::kMaxCtas) grid = b2::kMaxCtas;  // more rows per rank: each CTA loops over several
-  int threads = 64;  // one 8-element vector per thread per row up to dim 4096
-  while (threads < 512 && threads < dim / 8) threads *= 2;
-  const bool multi = R > grid;
+  // Decode-sized calls (a rank owns at most kMaxCtas rows): one CTA per owned row, one
+  // 8-element vector per thread (dim / 8 threads), at least 64 CTAs for the copy-out.
+  // Prefill-sized calls: CTAs of dim / 32 threads (four vectors per thread, so a row's 8
+  // sources x 4 loads are in flight per thread), as many as can be resident at once, each
+  // looping over its share of the owned rows; rows then proceed in parallel instead of
+  // one per CTA of a 128-CTA grid.  Every CTA of the grid must be resident together: part
+  // C waits for rows that other ranks' CTAs reduce, so a CTA that never got an SM could
+  // stall every rank until the timeout.
+  int grid, threads;
+  bool multi;
+  if (R <= b2::kMaxCtas) {
+    grid = R < 64 ? 64 : R;
+    threads = 64;
+    while (threads < 512 && threads < dim / 8) threads *= 2;
+    multi = false;
+  } else {
+    threads = 64;
+    while (threads < 512 && threads * 32 < dim) threads *= 2;
+    // resident CTAs per SM: the smaller of the two instantiations the grid may run
+    int occ = 1 << 30;
+    const void* fns[2] = {
+        dtype == B2_BF16 ? (const void*)b2::allreduce_rmsnorm_sharded_kernel<__nv_bfloat16, true>
+                         : (const void*)b2::allreduce_rmsnorm_sharded_kernel<float, true>,
+        dtype == B2_BF16 ? (const void*)b2::allreduce_rmsnorm_sharded_kernel<__nv_bfloat16, false>
+                         : (const void*)b2::allreduce_rmsnorm_sharded_kernel<float, false>};
+    for (const void* fn : fns) {
+      int o = 0;
+      B2_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, threads, 0));
+      occ = o < occ ? o : occ;
+    }
+    const long resident = (long)(occ < 1 ? 1 : occ) * b2::sm_count();
+    grid = (int)(R < resident ? R : resident);
+    multi = R > grid;
+  }
   if (dtype == B2_BF16)
     B2_TRY_CUDA(b2::launch_pdl(multi ? b2::allreduce_rmsnorm_sharded_kernel<__nv_bfloat16, true>
                                      : b2::allreduce_rmsnorm_sharded_kernel<__nv_bfloat16, false>,

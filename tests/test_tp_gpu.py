@@ -76,12 +76,14 @@ def test_row_parallel_linear_with_in_memory_comm():
 
 
 @pytest.mark.skipif(NGPU < 2, reason="needs 2 GPUs")
-def test_sharded_allreduce_rmsnorm_more_rows_than_ctas():
-    """A prefill-sized call: 600 rows give each of 2 ranks 300 rows, more than the kernel's
-    128 CTAs, so every CTA reduces several rows.  Against torch float32 on the same inputs."""
+@pytest.mark.parametrize("T", [600, 12000])
+def test_sharded_allreduce_rmsnorm_more_rows_than_ctas(T):
+    """Prefill-sized calls: 600 rows give each of 2 ranks 300 rows (one CTA per row, more
+    rows than the decode grid's 128 CTAs); 12000 rows give 6000, more than can be resident,
+    so every CTA reduces several rows.  Against torch float32 on the same inputs."""
     from pythonintern_b200.tensor_parallel.comm import DistributedCommunicator
     from pythonintern_b200.tensor_parallel.layers import RowParallelLinear
-    T, K, H, eps = 600, 256, 512, 1e-5
+    K, H, eps = 256, 512, 1e-5
     gen = torch.Generator().manual_seed(3)
     x = torch.randn(T, K, generator=gen).to(torch.bfloat16)
     w = (torch.randn(K, H, generator=gen) * 0.05).to(torch.bfloat16)
