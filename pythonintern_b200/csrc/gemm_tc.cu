@@ -337,6 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint32_t tmem_slot;
   __shared__ int s_last;
   __shared__ float s_inv[BN];  // deferred RMSNorm: per-token scale of the current unit
+  __shared__ void* s_row[BN];  // per token of the current unit: its output row (after the scatter)
 
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -493,10 +494,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.splits == 1) {
         const int64_t col = (int64_t)seg_col + n;
         const float bv = (nok && p.bias) ? p.bias[col] : 0.f;
-        if (p.row_ss) {
-          for (int c = threadIdx.x - 64; c < ncols; c += 128) s_inv[c] = row_inv(p, m0 + c);
-          epilogue_sync();
+        // Row addresses once per unit: the tensor-parallel scatter's owner rank and slot
+        // (a division and two loads) would otherwise be recomputed for every element.
+        for (int c = threadIdx.x - 64; c < ncols; c += 128) {
+          int64_t idx;
+          void* base = out_base(p.y, p.y_dtype, p.ldy, p.sc_table, p.sc_epoch, p.sc_R, p.sc_src, p.sc_world,
+                                m0 + c, 0, &idx);
+          s_row[c] = static_cast<char*>(base) + idx * (p.y_dtype == B2_BF16 ? 2 : 4);
+          if (p.row_ss) s_inv[c] = row_inv(p, m0 + c);
         }
+        epilogue_sync();
         for (int c0 = 0; c0 < ncols; c0 += 16) {
           float v[16];
           tmem_ld16(acc + c0, v);
@@ -517,13 +524,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (nok) {
 #pragma unroll
             for (int e = 0; e < 16; ++e)
-              if (c0 + e < ncols) store_out(p, m0 + c0 + e, col, v[e] + bv);
+              if (c0 + e < ncols) st_dyn(s_row[c0 + e], p.y_dtype, (size_t)col, v[e] + bv);
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
-        if (p.row_ss) epilogue_sync();  // s_inv is rewritten by the next unit
+        epilogue_sync();  // s_row / s_inv are rewritten by the next unit
       } else {
         // Split-K: publish this split's float32 tile ([column][128 rows], gate then up for
         // SwiGLU), release TMEM, and let the last split of the tile reduce.
