@@ -9,9 +9,16 @@ row-parallel all-reduce runs over NVLink peer memory).  Weights are N(0, 0.02)
 and the KV cache is random (synthetic data; there is no checkpoint or dataset).
 
   python bench.py --gpus N --steps K --warmup W           # this framework
-  python bench.py --impl reference --steps K --warmup W   # reference CPU algorithm
+  python bench.py --impl reference --steps K --warmup W   # the reference's CPU path (restated)
   python bench.py --workload prefill                      # batched varlen prefill (below)
+  python bench.py --workload mixed                        # 16 x 1024 prefills + 240 decodes in one step
+  python bench.py --workload tinyllama                    # TinyLlama, 64 requests x 128 new tokens
   torchrun --nproc-per-node N bench.py --workload allreduce   # row-parallel all-reduce (below)
+
+Before timing, the decode workload checks an 8B-shape layer at this TP degree against
+the oracle's fixture and, at TP <= 2, the Tiny LLaMA tokens against the reference's own
+(the ``parity`` object; a failure exits non-zero).  At TP > 1 the line also carries the
+row-parallel sweep (``fused_allreduce_sweep``: T in 1..4096 against NCCL).
 
 One JSON line on rank 0:
   value        decode tokens/s with inputs resident in HBM (CUDA events, max over ranks)
@@ -19,9 +26,10 @@ One JSON line on rank 0:
                StepRequests: pinned H2D of the step's inputs and D2H of the sampled
                tokens and top logits inside the timed region
   roofline     the dominant kernel's achieved HBM GB/s vs the measured copy peak
-  cpu_baseline the oracle restatement of the reference's CPU path on this host's
-               cores, on a bounded sample (one decoder layer of a few sequences),
-               extrapolated to a full step
+  cpu_baseline the reference's CPU path restated on torch CPU (oracle/grpc_tp.py) on
+               this host's cores: one decoder layer of the full batch plus 1/8 of
+               the lm_head, extrapolated to a full step (rank 0 at N=1); the
+               reference arm runs it at TP = N over the reference's gRPC all-reduce
 
 ``--workload prefill`` measures the other half of a serving step instead: the
 Mistral-7B shape (vocab 32000), 16 prompts of 1024 tokens prefilled in ONE batched
