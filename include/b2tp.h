@@ -210,6 +210,19 @@ int b2_prefill_attention(const void* q, int64_t ld_q, int n_rows, int nq, int nk
                          const int32_t* seq_ctx0, int n_seqs, float scale, void* out, int64_t ld_out, int dtype,
                          int32_t* status, b2_stream_t stream);
 
+/* The same causal prefill attention on the 5th-generation tensor cores: S = Q K^T and
+ * P V accumulated in TMEM by tcgen05.mma, Q/K/V tiles fed by TMA from q and the paged pool,
+ * softmax and the output rescaling on the CUDA cores.  Replaces the same reference code as
+ * b2_prefill_attention (engine/model/attention.py:166-174, :211-228).  bf16, head_dim 128,
+ * block_size 16, nq/nkv in {1,2,4,8}; q/out rows and the pool 16-byte aligned; other shapes
+ * return B2_EINVAL or B2_ENOTSUP without launching.  b2_prefill_attention uses this kernel
+ * for the shapes it serves. */
+int b2_prefill_attention_tc(const void* q, int64_t ld_q, int n_rows, int nq, int nkv, int head_dim,
+                            const void* k_cache, const void* v_cache, int layer, int num_blocks, int block_size,
+                            const int32_t* block_tables, int table_stride, const int32_t* seq_start,
+                            const int32_t* seq_ctx0, int n_seqs, float scale, void* out, int64_t ld_out, int dtype,
+                            int32_t* status, b2_stream_t stream);
+
 /* ---------------------------------------------------------------- greedy sampling
  * out[r] = first index of the maximum of logits[r, 0:cols]   (execution_engine.py:103,133) */
 int b2_argmax(const float* logits, int64_t ld, int rows, int cols, int64_t* out, b2_stream_t stream);

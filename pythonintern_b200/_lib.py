@@ -58,6 +58,9 @@ _SIGS = {
     "b2_prefill_attention": (_c_int, [_c_void_p, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
                                       _c_int, _c_int, _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_int,
                                       _c_float, _c_void_p, _c_i64, _c_int, _c_void_p, _c_void_p]),
+    "b2_prefill_attention_tc": (_c_int, [_c_void_p, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
+                                         _c_int, _c_int, _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_int,
+                                         _c_float, _c_void_p, _c_i64, _c_int, _c_void_p, _c_void_p]),
     "b2_argmax": (_c_int, [_c_void_p, _c_i64, _c_int, _c_int, _c_void_p, _c_void_p]),
     "b2_comm_handle_bytes": (_c_size, []),
     "b2_comm_create": (_c_int, [_c_int, _c_int, _c_size, ctypes.POINTER(_c_void_p)]),
@@ -134,7 +137,7 @@ _LAUNCHING = {"b2_embedding", "b2_rmsnorm", "b2_linear", "b2_linear_qkv", "b2_li
               "b2_rope_kv_write", "b2_paged_attention", "b2_argmax", "b2_allreduce_sum", "b2_allreduce_rmsnorm",
               "b2_row_parallel_linear", "b2_allreduce_rmsnorm_sharded", "b2_paged_attention_noalloc",
               "b2_argmax_allgather", "b2_linear_residual_norm", "b2_linear_qkv_rownorm", "b2_linear_swiglu_rownorm",
-              "b2_linear_qkv_rope_kv", "b2_prefill_attention"}
+              "b2_linear_qkv_rope_kv", "b2_prefill_attention", "b2_prefill_attention_tc"}
 
 
 def check(rc: int, what: str = ""):

@@ -19,7 +19,7 @@ INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libb2tp.so")
 
-SOURCES = ["api.cu", "norm.cu", "rope_kv.cu", "attention.cu", "gemm_simt.cu", "gemm_tc.cu", "gemm.cu", "comm.cu"]
+SOURCES = ["api.cu", "norm.cu", "rope_kv.cu", "attention.cu", "gemm_simt.cu", "gemm_tc.cu", "gemm.cu", "comm.cu", "prefill_tc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I", INCLUDE, "-I", CSRC]

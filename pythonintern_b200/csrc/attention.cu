@@ -23,6 +23,10 @@
 #include "common.cuh"
 
 namespace b2 {
+int prefill_attention_tc(const void* q, int64_t ld_q, int n_rows, int nq, int nkv, const void* k_cache,
+                         const void* v_cache, int64_t layer_off, int num_blocks, const int32_t* tables,
+                         int table_stride, const int32_t* seq_start, const int32_t* seq_ctx0, int n_seqs,
+                         float scale, void* out, int64_t ld_out, int32_t* status, cudaStream_t stream);
 
 struct AttnParams {
   const void* q;
@@ -1043,6 +1047,27 @@ int b2_paged_attention_noalloc(const void* q, int64_t ld_q, int n_rows, int nq, 
                             dtype, scratch, scratch ? b2::kNoAllocScratchBytes : 0, num_splits, status, stream);
 }
 
+
+int b2_prefill_attention_tc(const void* q, int64_t ld_q, int n_rows, int nq, int nkv, int head_dim,
+                            const void* k_cache, const void* v_cache, int layer, int num_blocks, int block_size,
+                            const int32_t* block_tables, int table_stride, const int32_t* seq_start,
+                            const int32_t* seq_ctx0, int n_seqs, float scale, void* out, int64_t ld_out, int dtype,
+                            int32_t* status, b2_stream_t stream) {
+  B2_CHECK_ARG(n_rows >= 0 && n_seqs >= 0 && nq > 0 && nkv > 0 && nq % nkv == 0,
+               "b2_prefill_attention_tc: bad sizes");
+  B2_CHECK_ARG(dtype == B2_BF16 && head_dim == 128 && block_size == 16,
+               "b2_prefill_attention_tc: bf16, head_dim 128 and block_size 16 only");
+  B2_CHECK_ARG(num_blocks > 0 && table_stride > 0 && layer >= 0, "b2_prefill_attention_tc: bad cache geometry");
+  B2_CHECK_ARG(ld_q >= (int64_t)nq * head_dim && ld_out >= (int64_t)nq * head_dim,
+               "b2_prefill_attention_tc: row strides too small");
+  B2_CHECK_ARG(nkv <= 65535, "b2_prefill_attention_tc: nkv %d > 65535", nkv);
+  if (n_rows == 0 || n_seqs == 0) return B2_OK;
+  B2_CHECK_ARG(q && k_cache && v_cache && block_tables && seq_start && out && status,
+               "b2_prefill_attention_tc: null pointer");
+  const int64_t layer_off = (int64_t)layer * num_blocks * block_size * nkv * head_dim;
+  return b2::prefill_attention_tc(q, ld_q, n_rows, nq, nkv, k_cache, v_cache, layer_off, num_blocks, block_tables,
+                                  table_stride, seq_start, seq_ctx0, n_seqs, scale, out, ld_out, status, stream);
+}
 
 int b2_prefill_attention(const void* q, int64_t ld_q, int n_rows, int nq, int nkv, int head_dim,
                          const void* k_cache, const void* v_cache, int layer, int num_blocks, int block_size,

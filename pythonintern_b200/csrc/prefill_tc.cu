@@ -1,0 +1,487 @@
+// Causal varlen prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM), head_dim 128.
+//
+// engine/model/attention.py:166-174 and :211-228 for a prefill: every prompt token attends
+// to the keys of its own sequence at positions 0..pos (the causal mask of :219-222), for
+// every prompt of a step in one launch (the reference runs one forward per prompt,
+// execution_engine.py:85-111).  Rows [seq_start[s], seq_start[s+1]) are sequence s's
+// tokens at positions seq_ctx0[s] + (row - seq_start[s]); their K/V are already in the
+// paged pool (block-table row s).
+//
+// A CTA owns one kv head g and a tile of QT = 128 / REP consecutive tokens of one
+// sequence: its 128 MMA rows are the (token, query head) pairs that share g, row
+// m = token * REP + head, so every K/V tile serves QT tokens x REP heads.  Per CTA:
+//
+//   warp 0 / lane 0 : TMA producer.  Q once (a 3D box [QT tokens][REP heads][64 dims],
+//                     twice for the two 64-dim halves), then per KV tile of 64 keys the
+//                     four 16-token pool blocks of K and of V (2D boxes [16 rows][64 dims]
+//                     through the block table) into a 3-stage ring; 128-byte swizzle, no
+//                     multicast.
+//   warp 1 / lane 0 : MMA issuer.  S(j) = Q K(j)^T (M=128, N=64, K=128) into one of two
+//                     TMEM S buffers; after S(j+1) is issued, PV(j) = P(j) V(j) (M=128,
+//                     N=128, K=64; V read in place, MN-major) into one of two TMEM PV
+//                     buffers.  tcgen05.commit signals each result and frees the K/V stage.
+//   warps 2-5       : one thread per MMA row (TMEM lane).  Softmax of S(j) in the log2
+//                     domain with the causal mask, P(j) to shared memory in bf16 (the A
+//                     operand of PV(j)), then O = O * exp2(m_old - m_new) + PV(j-1) in
+//                     registers; finally O / l to global memory.
+//
+// S(j+1) and PV(j-1) run on the tensor cores while the threads work on S(j).  Every wait
+// is bounded by %globaltimer; a timeout raises B2_DEV_PIPE_TIMEOUT and the CTA drains its
+// copies, frees TMEM and returns.  A block id outside the pool raises B2_DEV_RANGE and its
+// keys are read from block 0 and masked (so no uninitialised shared memory is ever used).
+#include <mutex>
+#include <set>
+
+#include "common.cuh"
+#include "tc_ptx.cuh"
+
+namespace b2 {
+namespace pftc {
+
+using namespace b2::tc;
+
+constexpr int HD = 128;
+constexpr int ROWS = 128;                              // MMA M: (token, head) rows per CTA
+constexpr int KT = 64;                                 // keys per KV tile (4 pool blocks)
+constexpr int ST = 3;                                  // KV ring stages
+constexpr int kThreads = 192;                          // producer, MMA, 4 softmax warps
+constexpr uint32_t HALF = KT * 64 * 2;                 // 8 KB: 64 keys x 64 dims
+constexpr uint32_t STAGE = 4 * HALF;                   // K lo | K hi | V lo | V hi
+constexpr uint32_t P_BYTES = ROWS * KT * 2;            // 16 KB
+constexpr uint32_t Q_HALF = ROWS * 64 * 2;             // 16 KB
+// Layout (1024-byte aligned): the K/V ring first, then P[2], then Q lo | Q hi.
+constexpr uint32_t OFF_P = ST * STAGE;
+constexpr uint32_t OFF_Q = OFF_P + 2 * P_BYTES;
+constexpr size_t SMEM = OFF_Q + 2 * Q_HALF + 1024;
+constexpr uint32_t TMEM_COLS = 512;                    // S[2] (64 each) + PV[2] (128 each), rounded up
+constexpr uint32_t COL_S = 0, COL_PV = 128;
+
+struct Params {
+  int n_rows, nq, nkv;
+  int num_blocks;
+  const int32_t* tables;
+  int table_stride;
+  const int32_t* seq_start;
+  const int32_t* seq_ctx0;
+  int n_seqs;
+  float scale_log2;
+  void* out;
+  int64_t ld_out;
+  int32_t* status;
+};
+
+// Shared-memory descriptor of an MN-major operand with 128-byte swizzle: 64-element rows
+// along N (128 bytes), 8-row groups along K `sbo` bytes apart, the next 64 N-elements
+// `lbo` bytes on (sm_100 descriptor version 1).
+__device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+template <int REP>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const Params p) {
+  constexpr int QT = ROWS / REP;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t q_full;
+  __shared__ __align__(8) uint64_t kv_full[ST];
+  __shared__ __align__(8) uint64_t kv_empty[ST];
+  __shared__ __align__(8) uint64_t s_full[2];
+  __shared__ __align__(8) uint64_t s_empty[2];
+  __shared__ __align__(8) uint64_t p_full[2];
+  __shared__ __align__(8) uint64_t pv_full[2];
+  __shared__ __align__(8) uint64_t pv_empty[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+
+  pdl_wait();  // the metadata, q and the pool may come from the preceding kernels
+  pdl_trigger();
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.y;
+
+  // (sequence, tile) of this CTA: tiles are numbered sequence by sequence, each sequence's
+  // last (longest) tile first; every warp computes the same answer (warp prefix sums).
+  int seq = -1, tile = 0;
+  {
+    int base = 0;
+    for (int s0 = 0; s0 < p.n_seqs && seq < 0; s0 += 32) {
+      const int s = s0 + lane;
+      int nt = 0;
+      if (s < p.n_seqs) {
+        const int len = p.seq_start[s + 1] - p.seq_start[s];
+        nt = len > 0 ? (len + QT - 1) / QT : 0;
+      }
+      int inc = nt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += v;
+      }
+      const int total = __shfl_sync(0xffffffffu, inc, 31);
+      const int bx = (int)blockIdx.x - base;
+      if (bx < total) {
+        const unsigned hit = __ballot_sync(0xffffffffu, bx < inc);
+        const int l = __ffs(hit) - 1;
+        const int inc_l = __shfl_sync(0xffffffffu, inc, l);
+        const int nt_l = __shfl_sync(0xffffffffu, nt, l);
+        seq = s0 + l;
+        tile = bx - (inc_l - nt_l);
+      }
+      base += total;
+    }
+  }
+  if (seq < 0) return;  // past the last tile (the grid is an upper bound); nothing allocated yet
+  const int rs = p.seq_start[seq], re = p.seq_start[seq + 1];
+  const int ctx0 = p.seq_ctx0 ? p.seq_ctx0[seq] : 0;
+  if (rs < 0 || re > p.n_rows || ctx0 < 0) {
+    if (threadIdx.x == 0) raise_status(p.status, B2_DEV_RANGE);
+    return;
+  }
+  const int len = re - rs;
+  const int ntile = (len + QT - 1) / QT;
+  const int t0 = (ntile - 1 - tile) * QT;     // first token of the tile within its sequence
+  const int nt = min(QT, len - t0);           // tokens in the tile (>= 1)
+  const int last_pos = ctx0 + t0 + nt - 1;    // the last position any row attends to
+  const int n_kv = last_pos / KT + 1;         // KV tiles of 64 keys
+  const int32_t* table = p.tables + (int64_t)seq * p.table_stride;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], 4);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&pv_full[b], 1);
+      mbar_init(&pv_empty[b], 4);
+    }
+    mbar_init(&drain_bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      const uint64_t pol_q = policy_evict_first();
+      const uint64_t pol_kv = policy_evict_last();  // K/V tiles are re-read by the sequence's other tiles
+      mbar_arrive_expect_tx(&q_full, 2 * Q_HALF);
+      tma_load_3d(smem + OFF_Q, &tmQ, &q_full, 0, g * REP, rs + t0, pol_q);
+      tma_load_3d(smem + OFF_Q + Q_HALF, &tmQ, &q_full, 64, g * REP, rs + t0, pol_q);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_kv && ok; ++j, ++issued) {
+        const int st = j % ST;
+        if (!mbar_wait(&kv_empty[st], ((uint32_t)(j / ST) & 1u) ^ 1u)) {
+          raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+          ok = false;
+          break;
+        }
+        uint8_t* sb = smem + (size_t)st * STAGE;
+        mbar_arrive_expect_tx(&kv_full[st], STAGE);
+        for (int b = 0; b < KT / 16; ++b) {
+          const int bi = j * (KT / 16) + b;
+          int blk = bi < p.table_stride ? table[bi] : -1;
+          if (blk < 0 || blk >= p.num_blocks) {
+            // A block holding keys some row attends to must exist; past the last position
+            // the keys are masked and any valid block serves as filler.
+            if (bi * 16 <= last_pos) raise_status(p.status, B2_DEV_RANGE);
+            blk = 0;
+          }
+          const int y = blk * 16;
+          tma_load_2d(sb + b * 2048, &tmK, &kv_full[st], g * HD, y, pol_kv);
+          tma_load_2d(sb + HALF + b * 2048, &tmK, &kv_full[st], g * HD + 64, y, pol_kv);
+          tma_load_2d(sb + 2 * HALF + b * 2048, &tmV, &kv_full[st], g * HD, y, pol_kv);
+          tma_load_2d(sb + 3 * HALF + b * 2048, &tmV, &kv_full[st], g * HD + 64, y, pol_kv);
+        }
+      }
+      // Copies still in flight (only after an aborted pipeline) land before the CTA exits.
+      mbar_wait(&q_full, 0, 100000000ull);
+      for (int st = 0; st < ST && st < issued; ++st) {
+        const int last_i = st + ((issued - 1 - st) / ST) * ST;
+        mbar_wait(&kv_full[st], (uint32_t)(last_i / ST) & 1u, 100000000ull);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = instr_desc_bf16(ROWS, KT);
+      constexpr uint32_t idesc_pv = instr_desc_bf16(ROWS, HD) | (1u << 16);  // B (V) MN-major
+      const uint32_t q_addr = smem_u32(smem + OFF_Q);
+      bool ok = mbar_wait(&q_full, 0);
+      if (!ok) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+      auto issue_pv = [&](int i) -> bool {
+        const int b = i & 1;
+        if (!mbar_wait(&p_full[b], (uint32_t)(i >> 1) & 1u) ||
+            !mbar_wait(&pv_empty[b], ((uint32_t)(i >> 1) & 1u) ^ 1u)) {
+          raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+          return false;
+        }
+        tc_fence_after();
+        const uint32_t p_addr = smem_u32(smem + OFF_P + b * P_BYTES);
+        const uint32_t v_addr = smem_u32(smem + (size_t)(i % ST) * STAGE + 2 * HALF);
+#pragma unroll
+        for (int kk = 0; kk < KT / 16; ++kk)  // 16 keys per MMA: +32 bytes of P rows, +2 KB of V rows
+          umma_bf16(tmem + COL_PV + b * HD, smem_desc_sw128(p_addr) + 2 * kk,
+                    smem_desc_sw128_mn(v_addr + kk * 2048, HALF, 1024), idesc_pv, kk > 0 ? 1u : 0u);
+        umma_commit(&pv_full[b]);
+        umma_commit(&kv_empty[i % ST]);
+        return true;
+      };
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j % ST, b = j & 1;
+        if (!mbar_wait(&kv_full[st], (uint32_t)(j / ST) & 1u) ||
+            !mbar_wait(&s_empty[b], ((uint32_t)(j >> 1) & 1u) ^ 1u)) {
+          raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + (size_t)st * STAGE);
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + COL_S + b * KT, smem_desc_sw128(q_addr + half * Q_HALF) + 2 * kk,
+                      smem_desc_sw128(k_addr + half * HALF) + 2 * kk, idesc_s, (half | kk) ? 1u : 0u);
+        umma_commit(&s_full[b]);
+        if (j >= 1 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && n_kv >= 1) issue_pv(n_kv - 1);
+      umma_commit(&drain_bar);  // every MMA issued by this thread has completed once it fires
+      mbar_wait(&drain_bar, 0, 100000000ull);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax / accumulation: one thread per MMA row
+    const int quarter = warp & 3;
+    const int m = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int tk = m / REP, h = m % REP;
+    const bool row_ok = tk < nt;
+    const int pos = ctx0 + t0 + tk;  // this row's token position (the last key it attends to)
+    float o[HD];
+#pragma unroll
+    for (int c = 0; c < HD; ++c) o[c] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f, m_o = -INFINITY;
+    float m_tile[2] = {-INFINITY, -INFINITY};
+    bool ok = true;
+    auto accumulate = [&](int i) {  // O = O * exp2(m_o - m(i)) + PV(i)
+      const int b = i & 1;
+      const bool done = mbar_wait(&pv_full[b], (uint32_t)(i >> 1) & 1u);
+      if (!done) {
+        if (lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+        ok = false;
+      }
+      tc_fence_after();
+      const float mi = m_tile[b];
+      const float corr = (m_o == -INFINITY) ? 0.f : exp2f(m_o - mi);
+#pragma unroll
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + lane_off + COL_PV + b * HD + c0, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[c0 + e] = done ? o[c0 + e] * corr + v[e] : o[c0 + e];
+      }
+      if (done) m_o = mi;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pv_empty[b]);
+    };
+    for (int j = 0; j < n_kv && ok; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&s_full[b], (uint32_t)(j >> 1) & 1u)) {
+        if (lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t s_addr = tmem + lane_off + COL_S + b * KT;
+      const int k0 = j * KT;
+      // pass 1: the row maximum over the unmasked keys of this tile
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c0 = 0; c0 < KT; c0 += 32) {
+        float v[32];
+        tmem_ld32(s_addr + c0, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (row_ok && k0 + c0 + e <= pos) mx = fmaxf(mx, v[e] * p.scale_log2);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      // pass 2: P = exp2(s - m_new) in bf16 into the swizzled A-operand rows of P[b]
+      uint8_t* prow = smem + OFF_P + b * P_BYTES + m * 128;
+      float lsum = 0.f;
+#pragma unroll
+      for (int c0 = 0; c0 < KT; c0 += 32) {
+        float v[32];
+        tmem_ld32(s_addr + c0, v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {  // 8 keys = one 16-byte chunk
+          uint32_t w[4];
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            float pr[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int e = q * 8 + e2 * 2 + u;
+              const bool valid = row_ok && k0 + c0 + e <= pos && m_new != -INFINITY;
+              pr[u] = valid ? exp2f(v[e] * p.scale_log2 - m_new) : 0.f;
+              lsum += pr[u];
+            }
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(pr[0], pr[1]);
+            w[e2] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+          const int chunk = c0 / 8 + q;
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ (m & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      l_run = (m_run == -INFINITY ? 0.f : l_run * exp2f(m_run - m_new)) + lsum;
+      m_run = m_new;
+      m_tile[b] = m_new;
+      fence_proxy_async_smem();  // P[b] written by these threads is read by the tensor cores
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_empty[b]);
+        mbar_arrive(&p_full[b]);
+      }
+      if (j >= 1) accumulate(j - 1);
+    }
+    if (ok && n_kv >= 1) accumulate(n_kv - 1);
+    // O / l to global memory: the row's 128 dims, 16-byte stores
+    if (ok && row_ok) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)(rs + t0 + tk) * p.ld_out +
+                           (int64_t)(g * REP + h) * HD;
+#pragma unroll
+      for (int c = 0; c < HD; c += 8) {
+        uint32_t w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(o[c + 2 * u] * inv, o[c + 2 * u + 1] * inv);
+          w[u] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        *reinterpret_cast<uint4*>(dst + c) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+
+  // ---------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+static int allow_smem_once(const void* fn, size_t bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  B2_TRY_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({fn, dev})) return B2_OK;
+  B2_TRY_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  done.insert({fn, dev});
+  return B2_OK;
+}
+
+static int encode(CUtensorMap* m, const void* ptr, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                  const cuuint32_t* box) {
+  auto fn = encode_fn();
+  if (!fn) return fail(B2_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(ptr), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B2_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return B2_OK;
+}
+
+}  // namespace pftc
+
+// Launches the tensor-core prefill attention (bf16, head_dim 128).  Returns B2_ENOTSUP,
+// launching nothing, for shapes it does not serve.
+int prefill_attention_tc(const void* q, int64_t ld_q, int n_rows, int nq, int nkv, const void* k_cache,
+                         const void* v_cache, int64_t layer_off, int num_blocks, const int32_t* tables,
+                         int table_stride, const int32_t* seq_start, const int32_t* seq_ctx0, int n_seqs,
+                         float scale, void* out, int64_t ld_out, int32_t* status, cudaStream_t stream) {
+  using namespace pftc;
+  const int rep = nq / nkv;
+  if (!(rep == 1 || rep == 2 || rep == 4 || rep == 8)) return fail(B2_ENOTSUP, "prefill tc: nq/nkv = %d", rep);
+  if (((uintptr_t)q % 16) || (ld_q % 8) || ((uintptr_t)k_cache % 16) || ((uintptr_t)v_cache % 16) ||
+      ((uintptr_t)out % 16) || (ld_out % 8))
+    return fail(B2_ENOTSUP, "prefill tc: q/out rows and the pool need 16-byte alignment");
+  Params p{};
+  p.n_rows = n_rows;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.num_blocks = num_blocks;
+  p.tables = tables;
+  p.table_stride = table_stride;
+  p.seq_start = seq_start;
+  p.seq_ctx0 = seq_ctx0;
+  p.n_seqs = n_seqs;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = out;
+  p.ld_out = ld_out;
+  p.status = status;
+  const int qt = ROWS / rep;
+  CUtensorMap mq, mk, mv;
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)nq, (cuuint64_t)n_rows};
+    const cuuint64_t strides[2] = {(cuuint64_t)HD * 2, (cuuint64_t)ld_q * 2};
+    const cuuint32_t box[3] = {64, (cuuint32_t)rep, (cuuint32_t)qt};
+    const int rc = encode(&mq, q, 3, dims, strides, box);
+    if (rc) return rc;
+  }
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)nkv * HD, (cuuint64_t)num_blocks * 16};
+    const cuuint64_t strides[1] = {(cuuint64_t)nkv * HD * 2};
+    const cuuint32_t box[2] = {64, 16};
+    const char* kb = static_cast<const char*>(k_cache) + layer_off * 2;
+    const char* vb = static_cast<const char*>(v_cache) + layer_off * 2;
+    int rc = encode(&mk, kb, 2, dims, strides, box);
+    if (rc) return rc;
+    rc = encode(&mv, vb, 2, dims, strides, box);
+    if (rc) return rc;
+  }
+  const dim3 grid(n_rows / qt + n_seqs, nkv);
+  auto go = [&](void (*k)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const Params)) -> int {
+    const int rc = allow_smem_once((const void*)k, SMEM);
+    if (rc) return rc;
+    B2_TRY_CUDA(launch_pdl(k, grid, dim3(kThreads), SMEM, stream, mq, mk, mv, p));
+    return B2_OK;
+  };
+  switch (rep) {
+    case 1: return go(prefill_attn_tc_kernel<1>);
+    case 2: return go(prefill_attn_tc_kernel<2>);
+    case 4: return go(prefill_attn_tc_kernel<4>);
+    default: return go(prefill_attn_tc_kernel<8>);
+  }
+}
+
+}  // namespace b2

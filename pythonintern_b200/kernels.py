@@ -303,13 +303,14 @@ def prefill_supported(dtype: torch.dtype, nq: int, nkv: int, head_dim: int, bloc
 def prefill_attention(q: torch.Tensor, nq: int, nkv: int, head_dim: int, k_cache: torch.Tensor,
                       v_cache: torch.Tensor, layer: int, block_tables: torch.Tensor, seq_start: torch.Tensor,
                       n_seqs: int, scale: float, seq_ctx0: Optional[torch.Tensor] = None,
-                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                      out: Optional[torch.Tensor] = None, tensor_cores: bool = False) -> torch.Tensor:
     """Causal attention of every prompt token of ``n_seqs`` sequences in one launch.
 
     Rows ``[seq_start[s], seq_start[s+1])`` of ``q`` are sequence s at positions
     ``seq_ctx0[s] + (row - seq_start[s])``; each attends to keys ``0..pos`` of its own
     sequence in the pool (block-table row s).  engine/model/attention.py:166-174,211-228,
     which the reference runs one sequence at a time (execution_engine.py:85-111).
+    ``tensor_cores`` calls the tcgen05 kernel directly (head_dim 128).
     """
     n_rows = q.shape[0]
     _, NB, bs, _, _ = k_cache.shape
@@ -317,11 +318,11 @@ def prefill_attention(q: torch.Tensor, nq: int, nkv: int, head_dim: int, k_cache
         out = torch.empty(n_rows, nq * head_dim, dtype=q.dtype, device=q.device)
     assert seq_start.dtype == torch.int32 and seq_start.numel() >= n_seqs + 1
     assert seq_ctx0 is None or (seq_ctx0.dtype == torch.int32 and seq_ctx0.numel() >= n_seqs)
-    check(_lib.lib().b2_prefill_attention(
+    name = "b2_prefill_attention_tc" if tensor_cores else "b2_prefill_attention"
+    check(getattr(_lib.lib(), name)(
         ptr(q), q.stride(0), n_rows, nq, nkv, head_dim, ptr(k_cache), ptr(v_cache), layer, NB, bs,
         ptr(block_tables), block_tables.shape[1], ptr(seq_start), ptr(seq_ctx0), n_seqs, float(scale),
-        ptr(out), out.stride(0), dtype_code(q.dtype), status_ptr(q.device), stream_ptr(q.device)),
-        "b2_prefill_attention")
+        ptr(out), out.stride(0), dtype_code(q.dtype), status_ptr(q.device), stream_ptr(q.device)), name)
     return out
 
 

@@ -113,6 +113,55 @@ def test_prefill_attention_vs_oracle(nq, nkv, hd):
         assert rel(got[r], want[r]) < 3e-2, r
 
 
+def _run_tc(q, kc, vc, tab, lens, ctx0, nq, nkv, hd):
+    pos, tidx, ctx, seq_start, last, c0 = prefill_layout(lens, ctx0)
+    T = q.shape[0]
+    return kernels.prefill_attention(q.view(T, nq * hd).to(DEV), nq, nkv, hd, kc.to(DEV), vc.to(DEV), 0,
+                                     torch.from_numpy(tab).to(DEV), torch.from_numpy(seq_start).to(DEV), len(lens),
+                                     1 / math.sqrt(hd), tensor_cores=True,
+                                     seq_ctx0=None if c0 is None else torch.from_numpy(c0).to(DEV))
+
+
+@pytest.mark.parametrize("nq,nkv", [(32, 8), (8, 1), (16, 2), (4, 4), (8, 4)])
+@pytest.mark.parametrize("lens,ctx0", [([1, 16, 17, 70, 130, 15, 64], [0, 0, 5, 0, 33, 16, 0]),
+                                       ([1024, 300, 513], [0, 200, 0])])
+def test_prefill_attention_tensor_cores_vs_oracle(nq, nkv, lens, ctx0):
+    """The tcgen05 kernel (S and P.V in TMEM, K/V tiles of 64 keys over a 3-stage TMA ring) per
+    row against the oracle, and against the mma.sync kernel on the same inputs."""
+    hd = 128
+    q, kc, vc, tables, tab = _case(lens, ctx0, nq, nkv, hd, seed=nq * 3 + len(lens))
+    out = _run_tc(q, kc, vc, tab, lens, ctx0, nq, nkv, hd)
+    torch.cuda.synchronize()
+    _lib.check_device_status(DEV, "prefill attention (tensor cores)")
+    if sum(lens) > 1000:
+        # the oracle's per-row loop is slow: check a spread of rows of every sequence
+        rows = sorted({0, 1, 15, 16, 63, 64, 65, 127, 128, 500, 1023, 1024, 1100, 1323, 1324, 1500, sum(lens) - 1})
+    else:
+        rows = list(range(sum(lens)))
+    want = _oracle_rows_subset(q, kc, vc, tables, lens, ctx0, rows)
+    got = to_np(out)[rows]
+    assert rel(got, want) < 1e-2
+    for i, r in enumerate(rows):
+        assert rel(got[i], want[i]) < 3e-2, r
+    ref = to_np(_run(q, kc, vc, tab, lens, ctx0, nq, nkv, hd))
+    assert rel(to_np(out), ref) < 1e-2
+
+
+def _oracle_rows_subset(q, kc, vc, tables, lens, ctx0, rows):
+    T, nq, hd = q.shape
+    nkv = kc.shape[3]
+    pool = oracle.KVPool(1, kc.shape[1], 16, nkv, hd)
+    pool.k[:] = kc.float().numpy()
+    pool.v[:] = vc.float().numpy()
+    pos, tidx, _, _, _, _ = prefill_layout(lens, ctx0)
+    row_tables = [tables[int(tidx[r])] for r in rows]
+    p = pos[rows]
+    knew = np.stack([pool.k[0][row_tables[i][p[i] // 16], p[i] % 16] for i in range(len(rows))])
+    vnew = np.stack([pool.v[0][row_tables[i][p[i] // 16], p[i] % 16] for i in range(len(rows))])
+    return oracle.decode_attention(q.float().numpy()[rows], knew, vnew, p, pool, 0, row_tables, 1 / math.sqrt(hd),
+                                   compat_pad=False)
+
+
 def test_prefill_attention_matches_reference_prefill_shape():
     """ctx0 = 0: the reference's own prefill (oracle.prefill_attention, one sequence per call)."""
     nq, nkv, hd = 32, 8, 128
