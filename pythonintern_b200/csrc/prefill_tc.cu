@@ -289,7 +289,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     auto accumulate = [&](int i) {  // O = O * exp2(m_o - m(i)) + PV(i)
       const int b = i & 1;
-      const bool done = mbar_wait(&pv_full[b], (uint32_t)(i >> 1) & 1u);
+      // warp-uniform verdict: the TMEM loads below are .sync.aligned
+      const bool done = __all_sync(0xffffffffu, mbar_wait(&pv_full[b], (uint32_t)(i >> 1) & 1u));
       if (!done) {
         if (lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
         ok = false;
@@ -311,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     for (int j = 0; j < n_kv && ok; ++j) {
       const int b = j & 1;
-      if (!mbar_wait(&s_full[b], (uint32_t)(j >> 1) & 1u)) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (uint32_t)(j >> 1) & 1u))) {
         if (lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
         ok = false;
         break;
