@@ -20,10 +20,12 @@
 //                     TMEM S buffers; after S(j+1) is issued, PV(j) = P(j) V(j) (M=128,
 //                     N=128, K=64; V read in place, MN-major) into one of two TMEM PV
 //                     buffers.  tcgen05.commit signals each result and frees the K/V stage.
-//   warps 2-5       : one thread per MMA row (TMEM lane).  Softmax of S(j) in the log2
-//                     domain with the causal mask, P(j) to shared memory in bf16 (the A
-//                     operand of PV(j)), then O = O * exp2(m_old - m_new) + PV(j-1) in
-//                     registers; finally O / l to global memory.
+//   warps 2-9       : two threads per MMA row (TMEM lane): warps w and w + 4 share a lane
+//                     quarter, each owning half of the row's 64 scores and 128 output dims.
+//                     Softmax of S(j) in the log2 domain with the causal mask (the two
+//                     halves exchange their row maxima through shared memory), P(j) to
+//                     shared memory in bf16 (the A operand of PV(j)), then
+//                     O = O * exp2(m_old - m_new) + PV(j-1) in registers; finally O / l.
 //
 // S(j+1) and PV(j-1) run on the tensor cores while the threads work on S(j).  Every wait
 // is bounded by %globaltimer; a timeout raises B2_DEV_PIPE_TIMEOUT and the CTA drains its
@@ -40,11 +42,30 @@ namespace pftc {
 
 using namespace b2::tc;
 
+// Named barrier over the softmax warps only (the producer and MMA warps keep running).
+__device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * 8) : "memory"); }
+// The same barrier, returning the AND of `pred` over all softmax threads, so that every
+// softmax warp leaves the main loop in the same iteration (a warp waiting at a named
+// barrier for a warp that already left would wait without bound).
+__device__ __forceinline__ bool softmax_all(bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"((uint32_t)pred), "n"(32 * 8)
+      : "memory");
+  return out != 0;
+}
+
 constexpr int HD = 128;
 constexpr int ROWS = 128;                              // MMA M: (token, head) rows per CTA
 constexpr int KT = 64;                                 // keys per KV tile (4 pool blocks)
 constexpr int ST = 3;                                  // KV ring stages
-constexpr int kThreads = 192;                          // producer, MMA, 4 softmax warps
+constexpr int kSoftWarps = 8;                          // two per TMEM lane quarter: each owns half a row
+constexpr int kThreads = 64 + 32 * kSoftWarps;         // producer, MMA, softmax warps
 constexpr uint32_t HALF = KT * 64 * 2;                 // 8 KB: 64 keys x 64 dims
 constexpr uint32_t STAGE = 4 * HALF;                   // K lo | K hi | V lo | V hi
 constexpr uint32_t P_BYTES = ROWS * KT * 2;            // 16 KB
@@ -99,6 +120,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t pv_empty[2];
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
+  __shared__ float s_red[2][2][ROWS];  // [tile parity][half][row]: the halves' row maxima
+  __shared__ float s_l[2][ROWS];       // [half][row]: the halves' final sums of probabilities
 
   pdl_wait();  // the metadata, q and the pool may come from the preceding kernels
   pdl_trigger();
@@ -160,10 +183,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 4);
-      mbar_init(&p_full[b], 4);
+      mbar_init(&s_empty[b], kSoftWarps);
+      mbar_init(&p_full[b], kSoftWarps);
       mbar_init(&pv_full[b], 1);
-      mbar_init(&pv_empty[b], 4);
+      mbar_init(&pv_empty[b], kSoftWarps);
     }
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
@@ -274,20 +297,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- softmax / accumulation: one thread per MMA row
-    const int quarter = warp & 3;
+    // ---------------- softmax / accumulation: two threads per MMA row
+    const int sw = warp - 2;                 // 0..7
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int half = sw >> 2;                // which half of the row's scores and dims
     const int m = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int tk = m / REP, h = m % REP;
     const bool row_ok = tk < nt;
     const int pos = ctx0 + t0 + tk;  // this row's token position (the last key it attends to)
-    float o[HD];
+    float o[HD / 2];
 #pragma unroll
-    for (int c = 0; c < HD; ++c) o[c] = 0.f;
+    for (int c = 0; c < HD / 2; ++c) o[c] = 0.f;
     float m_run = -INFINITY, l_run = 0.f, m_o = -INFINITY;
     float m_tile[2] = {-INFINITY, -INFINITY};
     bool ok = true;
-    auto accumulate = [&](int i) {  // O = O * exp2(m_o - m(i)) + PV(i)
+    auto accumulate = [&](int i) {  // O = O * exp2(m_o - m(i)) + PV(i), this thread's 64 dims
       const int b = i & 1;
       // warp-uniform verdict: the TMEM loads below are .sync.aligned
       const bool done = __all_sync(0xffffffffu, mbar_wait(&pv_full[b], (uint32_t)(i >> 1) & 1u));
@@ -296,16 +321,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
       }
       tc_fence_after();
+      uint32_t r0[32], r1[32];
+      const uint32_t a = tmem + lane_off + COL_PV + b * HD + half * (HD / 2);
+      tmem_ld32_nowait(a, r0);
+      tmem_ld32_nowait(a + 32, r1);
+      tmem_wait_ld();
       const float mi = m_tile[b];
       const float corr = (m_o == -INFINITY) ? 0.f : exp2f(m_o - mi);
+      if (done) {
 #pragma unroll
-      for (int c0 = 0; c0 < HD; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem + lane_off + COL_PV + b * HD + c0, v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[c0 + e] = done ? o[c0 + e] * corr + v[e] : o[c0 + e];
+        for (int e = 0; e < 32; ++e) {
+          o[e] = o[e] * corr + __uint_as_float(r0[e]);
+          o[32 + e] = o[32 + e] * corr + __uint_as_float(r1[e]);
+        }
+        m_o = mi;
       }
-      if (done) m_o = mi;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&pv_empty[b]);
@@ -315,48 +345,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (uint32_t)(j >> 1) & 1u))) {
         if (lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
         ok = false;
-        break;
       }
+      // both halves of every row must meet at the exchange below, so a failed wait still
+      // runs the barrier (with nothing valid) before leaving the loop
       tc_fence_after();
-      const uint32_t s_addr = tmem + lane_off + COL_S + b * KT;
-      const int k0 = j * KT;
-      // pass 1: the row maximum over the unmasked keys of this tile
+      uint32_t sr[32];
+      tmem_ld32_nowait(tmem + lane_off + COL_S + b * KT + half * 32, sr);
+      tmem_wait_ld();
+      const int k0 = j * KT + half * 32;
+      float sv[32];
       float mx = -INFINITY;
 #pragma unroll
-      for (int c0 = 0; c0 < KT; c0 += 32) {
-        float v[32];
-        tmem_ld32(s_addr + c0, v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (row_ok && k0 + c0 + e <= pos) mx = fmaxf(mx, v[e] * p.scale_log2);
+      for (int e = 0; e < 32; ++e) {
+        const bool valid = ok && row_ok && k0 + e <= pos;
+        sv[e] = valid ? __uint_as_float(sr[e]) * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, sv[e]);
       }
+      s_red[j & 1][half][m] = mx;
+      ok = softmax_all(ok);
+      mx = fmaxf(mx, s_red[j & 1][half ^ 1][m]);
+      if (!ok) break;
       const float m_new = fmaxf(m_run, mx);
-      // pass 2: P = exp2(s - m_new) in bf16 into the swizzled A-operand rows of P[b]
+      // P = exp2(s - m_new) in bf16 into this half's four 16-byte chunks of the swizzled row
       uint8_t* prow = smem + OFF_P + b * P_BYTES + m * 128;
       float lsum = 0.f;
 #pragma unroll
-      for (int c0 = 0; c0 < KT; c0 += 32) {
-        float v[32];
-        tmem_ld32(s_addr + c0, v);
+      for (int q = 0; q < 4; ++q) {
+        uint32_t w[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {  // 8 keys = one 16-byte chunk
-          uint32_t w[4];
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            float pr[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int e = q * 8 + e2 * 2 + u;
-              const bool valid = row_ok && k0 + c0 + e <= pos && m_new != -INFINITY;
-              pr[u] = valid ? exp2f(v[e] * p.scale_log2 - m_new) : 0.f;
-              lsum += pr[u];
-            }
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(pr[0], pr[1]);
-            w[e2] = *reinterpret_cast<uint32_t*>(&h2);
-          }
-          const int chunk = c0 / 8 + q;
-          *reinterpret_cast<uint4*>(prow + ((chunk ^ (m & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int e2 = 0; e2 < 4; ++e2) {
+          const int e = q * 8 + e2 * 2;
+          const float p0 = m_new == -INFINITY ? 0.f : exp2f(sv[e] - m_new);
+          const float p1 = m_new == -INFINITY ? 0.f : exp2f(sv[e + 1] - m_new);
+          lsum += p0 + p1;
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+          w[e2] = *reinterpret_cast<uint32_t*>(&h2);
         }
+        const int chunk = half * 4 + q;
+        *reinterpret_cast<uint4*>(prow + ((chunk ^ (m & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       l_run = (m_run == -INFINITY ? 0.f : l_run * exp2f(m_run - m_new)) + lsum;
       m_run = m_new;
@@ -371,13 +397,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j >= 1) accumulate(j - 1);
     }
     if (ok && n_kv >= 1) accumulate(n_kv - 1);
-    // O / l to global memory: the row's 128 dims, 16-byte stores
+    // the row's sum of probabilities is the sum of the two halves' (same running maximum)
+    s_l[half][m] = l_run;
+    softmax_sync();
+    const float l_tot = l_run + s_l[half ^ 1][m];
+    // O / l to global memory: this thread's 64 dims of the row, 16-byte stores
     if (ok && row_ok) {
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
       __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)(rs + t0 + tk) * p.ld_out +
-                           (int64_t)(g * REP + h) * HD;
+                           (int64_t)(g * REP + h) * HD + half * (HD / 2);
 #pragma unroll
-      for (int c = 0; c < HD; c += 8) {
+      for (int c = 0; c < HD / 2; c += 8) {
         uint32_t w[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
