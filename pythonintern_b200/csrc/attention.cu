@@ -1088,6 +1088,15 @@ int b2_prefill_attention(const void* q, int64_t ld_q, int n_rows, int nq, int nk
   B2_CHECK_ARG(((uintptr_t)q % 4) == 0 && (ld_q % 2) == 0 && ((uintptr_t)out % 4) == 0 && (ld_out % 2) == 0 &&
                    ((uintptr_t)k_cache % 16) == 0 && ((uintptr_t)v_cache % 16) == 0,
                "b2_prefill_attention: q/out need 4-byte rows, the cache 16-byte alignment");
+  if (head_dim == 128 && nkv <= 65535) {
+    // the tensor-core kernel serves head_dim 128 with 16-byte aligned rows; anything it
+    // declines (B2_ENOTSUP, nothing launched) runs on the mma.sync kernel below
+    const int64_t layer_off = (int64_t)layer * num_blocks * block_size * nkv * head_dim;
+    const int rc = b2::prefill_attention_tc(q, ld_q, n_rows, nq, nkv, k_cache, v_cache, layer_off, num_blocks,
+                                            block_tables, table_stride, seq_start, seq_ctx0, n_seqs, scale, out,
+                                            ld_out, status, stream);
+    if (rc != B2_ENOTSUP) return rc;
+  }
   b2::PrefillParams p{};
   p.q = q;
   p.ld_q = ld_q;

@@ -127,7 +127,7 @@ def _run_tc(q, kc, vc, tab, lens, ctx0, nq, nkv, hd):
                                        ([1024, 300, 513], [0, 200, 0])])
 def test_prefill_attention_tensor_cores_vs_oracle(nq, nkv, lens, ctx0):
     """The tcgen05 kernel (S and P.V in TMEM, K/V tiles of 64 keys over a 3-stage TMA ring) per
-    row against the oracle, and against the mma.sync kernel on the same inputs."""
+    row against the oracle (the mma.sync kernel keeps head_dim 32 and 64, tested above)."""
     hd = 128
     q, kc, vc, tables, tab = _case(lens, ctx0, nq, nkv, hd, seed=nq * 3 + len(lens))
     out = _run_tc(q, kc, vc, tab, lens, ctx0, nq, nkv, hd)
@@ -143,8 +143,8 @@ def test_prefill_attention_tensor_cores_vs_oracle(nq, nkv, lens, ctx0):
     assert rel(got, want) < 1e-2
     for i, r in enumerate(rows):
         assert rel(got[i], want[i]) < 3e-2, r
-    ref = to_np(_run(q, kc, vc, tab, lens, ctx0, nq, nkv, hd))
-    assert rel(to_np(out), ref) < 1e-2
+    # b2_prefill_attention runs this kernel for head_dim 128: the same bits
+    assert torch.equal(out, _run(q, kc, vc, tab, lens, ctx0, nq, nkv, hd))
 
 
 def _oracle_rows_subset(q, kc, vc, tables, lens, ctx0, rows):
