@@ -355,11 +355,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int k0 = j * KT + half * 32;
       float sv[32];
       float mx = -INFINITY;
+      if (ok && row_ok && k0 + 31 <= pos) {  // every key of this half-tile is visible (the common case)
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const bool valid = ok && row_ok && k0 + e <= pos;
-        sv[e] = valid ? __uint_as_float(sr[e]) * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, sv[e]);
+        for (int e = 0; e < 32; ++e) {
+          sv[e] = __uint_as_float(sr[e]) * p.scale_log2;
+          mx = fmaxf(mx, sv[e]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const bool valid = ok && row_ok && k0 + e <= pos;
+          sv[e] = valid ? __uint_as_float(sr[e]) * p.scale_log2 : -INFINITY;
+          mx = fmaxf(mx, sv[e]);
+        }
       }
       s_red[j & 1][half][m] = mx;
       ok = softmax_all(ok);
@@ -369,14 +377,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P = exp2(s - m_new) in bf16 into this half's four 16-byte chunks of the swizzled row
       uint8_t* prow = smem + OFF_P + b * P_BYTES + m * 128;
       float lsum = 0.f;
+      // a row with nothing visible yet keeps p = 0 (exp2(-inf - -inf) would be NaN)
+      const float m_sub = m_new == -INFINITY ? 0.f : m_new;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint32_t w[4];
 #pragma unroll
         for (int e2 = 0; e2 < 4; ++e2) {
           const int e = q * 8 + e2 * 2;
-          const float p0 = m_new == -INFINITY ? 0.f : exp2f(sv[e] - m_new);
-          const float p1 = m_new == -INFINITY ? 0.f : exp2f(sv[e + 1] - m_new);
+          const float p0 = exp2f(sv[e] - m_sub);      // sv = -inf (masked) gives 0
+          const float p1 = exp2f(sv[e + 1] - m_sub);
           lsum += p0 + p1;
           __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
           w[e2] = *reinterpret_cast<uint32_t*>(&h2);
