@@ -379,8 +379,8 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return (uint32_t)(row * MmaCfg<HD>::ROWB + ((chunk ^ (row & MmaCfg<HD>::SWZ)) << 4));
 }
 
-template <int HD, int REP>
-__global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnParams p) {
+template <int HD, int REP, int W, int STAGES>
+__global__ void __launch_bounds__(W * 32, W <= 4 ? 2 : 1) paged_attn_mma_kernel(AttnParams p) {
   pdl_wait();
   pdl_trigger();
   using C = MmaCfg<HD>;
@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnP
   const int blk1 = min(nblk, blk0 + bps);
   const int trow = p.table_index ? p.table_index[row] : row;
   const int32_t* table = p.tables + (int64_t)trow * p.table_stride;
-  const int n_w = blk1 - blk0 > warp ? (blk1 - blk0 - warp + kMmaWarps - 1) / kMmaWarps : 0;
+  const int n_w = blk1 - blk0 > warp ? (blk1 - blk0 - warp + W - 1) / W : 0;
 
   // Q fragments (A operand rows 0..7 = the REP heads, rows 8..15 = zero padding).
   uint32_t qa[HD / 16][2];
@@ -418,14 +418,14 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnP
   const int64_t tok_stride_b = (int64_t)p.nkv * HD * 2;  // bytes between token rows of the pool
   const char* kbase = reinterpret_cast<const char*>(p.k_cache) + (p.layer_off + (int64_t)g * HD) * 2;
   const char* vbase = reinterpret_cast<const char*>(p.v_cache) + (p.layer_off + (int64_t)g * HD) * 2;
-  const uint32_t wsm = smem_addr(smem) + (uint32_t)(warp * kMmaStages * C::STAGEB);
+  const uint32_t wsm = smem_addr(smem) + (uint32_t)(warp * STAGES * C::STAGEB);
 
   // Issue the copies of this warp's i-th block into ring slot (i % STAGES); a block id
   // outside the pool is not copied, and the main loop skips that block.
   auto issue = [&](int i) {
-    const int blk = table[blk0 + warp + i * kMmaWarps];
+    const int blk = table[blk0 + warp + i * W];
     if (blk < 0 || blk >= p.num_blocks) return;
-    const uint32_t st = wsm + (uint32_t)((i % kMmaStages) * C::STAGEB);
+    const uint32_t st = wsm + (uint32_t)((i % STAGES) * C::STAGEB);
     const int64_t blk_off = (int64_t)blk * bs * tok_stride_b;
 #pragma unroll
     for (int q = lane; q < 16 * C::CHUNKS; q += 32) {
@@ -442,16 +442,16 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnP
   float m_run = -INFINITY, l_run = 0.f;  // row qr statistics (per-lane partial l)
 
 #pragma unroll
-  for (int i = 0; i < kMmaStages - 1; ++i) {
+  for (int i = 0; i < STAGES - 1; ++i) {
     if (i < n_w) issue(i);
     cp_async_commit();
   }
   for (int i = 0; i < n_w; ++i) {
-    if (i + kMmaStages - 1 < n_w) issue(i + kMmaStages - 1);
+    if (i + STAGES - 1 < n_w) issue(i + STAGES - 1);
     cp_async_commit();
-    cp_async_wait<kMmaStages - 1>();
+    cp_async_wait<STAGES - 1>();
     __syncwarp();
-    const int bidx = blk0 + warp + i * kMmaWarps;
+    const int bidx = blk0 + warp + i * W;
     const int blk = table[bidx];
     const bool blk_ok = blk >= 0 && blk < p.num_blocks;
     if (!blk_ok) {
@@ -461,7 +461,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnP
       __syncwarp();
       continue;
     }
-    const uint32_t ks = wsm + (uint32_t)((i % kMmaStages) * C::STAGEB);
+    const uint32_t ks = wsm + (uint32_t)((i % STAGES) * C::STAGEB);
     const uint32_t vs = ks + C::BLKB;
 
     // S = Q K^T over 16 tokens: two 8-token n-tiles.
@@ -525,8 +525,8 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnP
   __syncthreads();  // the rings are idle; reuse them for the merge arrays
 
   float* sm_m = reinterpret_cast<float*>(smem);
-  float* sm_l = sm_m + kMmaWarps * REP;
-  float* sm_acc = sm_l + kMmaWarps * REP;
+  float* sm_l = sm_m + W * REP;
+  float* sm_acc = sm_l + W * REP;
   if (qr < REP) {
     if (qt == 0) {
       sm_m[warp * REP + qr] = m_run;
@@ -539,7 +539,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) paged_attn_mma_kernel(AttnP
     }
   }
   __syncthreads();
-  attn_finalize<__nv_bfloat16, HD, REP>(p, sm_m, sm_l, sm_acc, kMmaWarps, row, g, split, ctx);
+  attn_finalize<__nv_bfloat16, HD, REP>(p, sm_m, sm_l, sm_acc, W, row, g, split, ctx);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -820,22 +820,34 @@ static int allow_dynamic_smem(const void* fn, size_t bytes) {
   return B2_OK;
 }
 
-template <int HD>
-static int launch_mma_rep(int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {
-  using C = MmaCfg<HD>;
+template <int HD, int W, int STAGES>
+static int launch_mma_rep_cfg(int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {
+  const size_t smem = (size_t)W * STAGES * MmaCfg<HD>::STAGEB;
   auto go = [&](void (*k)(AttnParams)) -> int {
-    const int rc = allow_dynamic_smem((const void*)k, C::SMEM);
+    const int rc = allow_dynamic_smem((const void*)k, smem);
     if (rc) return rc;
-    B2_TRY_CUDA(launch_pdl(k, grid, dim3(kMmaWarps * 32), C::SMEM, s, p));
+    B2_TRY_CUDA(launch_pdl(k, grid, dim3(W * 32), smem, s, p));
     return B2_OK;
   };
   switch (rep) {
-    case 1: return go(paged_attn_mma_kernel<HD, 1>);
-    case 2: return go(paged_attn_mma_kernel<HD, 2>);
-    case 4: return go(paged_attn_mma_kernel<HD, 4>);
-    case 8: return go(paged_attn_mma_kernel<HD, 8>);
+    case 1: return go(paged_attn_mma_kernel<HD, 1, W, STAGES>);
+    case 2: return go(paged_attn_mma_kernel<HD, 2, W, STAGES>);
+    case 4: return go(paged_attn_mma_kernel<HD, 4, W, STAGES>);
+    case 8: return go(paged_attn_mma_kernel<HD, 8, W, STAGES>);
     default: return fail(B2_ENOTSUP, "b2_paged_attention: nq/nkv = %d not supported (1, 2, 4, 8)", rep);
   }
+}
+
+// Grids of at most one CTA per SM (few (row, kv head, split) triples, e.g. one kv head
+// per rank at TP=8) run 8 warps per CTA with 2-stage rings, so each SM still holds as
+// many warps as two 4-warp CTAs.  The configuration follows from the grid alone, so two
+// calls over the same shapes and split count (an eager call and a graph replay) give
+// the same bits; between the two configurations only the float summation order differs.
+template <int HD>
+static int launch_mma_rep(int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {
+  const long ctas = (long)grid.x * grid.y * grid.z;
+  if (ctas <= sm_count()) return launch_mma_rep_cfg<HD, 8, 2>(rep, p, grid, s);
+  return launch_mma_rep_cfg<HD, kMmaWarps, kMmaStages>(rep, p, grid, s);
 }
 
 static int launch_mma(int hd, int rep, const AttnParams& p, dim3 grid, cudaStream_t s) {

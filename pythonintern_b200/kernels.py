@@ -256,7 +256,8 @@ def rope_kv_write(qkv: torch.Tensor, nq: int, nkv: int, head_dim: int, rope_pos:
 
 def attention_splits(n_rows: int, nkv: int, max_ctx: int, block_size: int = 16, device=None) -> int:
     """KV split count: as many splits as keep every (row, kv head, split) CTA in ONE wave
-    (two attention CTAs are resident per SM), with at least 4 KV blocks per split.
+    (two attention CTAs are resident per SM), with at least 4 KV blocks per split; with
+    fewer (row, kv head) pairs than SMs, at most one CTA per SM and 4 splits.
 
     A second, partly filled wave leaves HBM idle at the tail (measured on B200 at context
     2048, batch 128: one kv head per row, 5 splits over 2.2 waves took 40 us, 2 splits in
@@ -271,6 +272,11 @@ def attention_splits(n_rows: int, nkv: int, max_ctx: int, block_size: int = 16, 
     if pairs >= slots:
         return 1
     nblk = 32 * max(1, math.ceil(max_ctx / (32 * block_size)))
+    if pairs < sms:
+        # at most one CTA per SM, where the kernel runs 8-warp CTAs; measured on B200 at
+        # context 2048: one kv head x 128 rows best with 1 split (26 us; 2 splits of 4-warp
+        # CTAs 30 us), 32 rows and a single row with 4 (11-12 us; 9 and 32 splits 17-25 us)
+        return max(1, min(sms // pairs, 4, max(1, nblk // 8)))
     s = min(slots // pairs, max(1, nblk // 4), 256)
     return max(1, s)
 
