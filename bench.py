@@ -978,6 +978,30 @@ def cpu_prefill_sample(cfg, P: int, seed: int):
     return t
 
 
+def cpu_job_estimate(cfg, prompt_lens, dec_batch, dec_ctx, dec_steps, seed):
+    """CPU time of a job of the reference's CPU path, extrapolated from bounded samples.
+
+    Prefill: one forward per prompt (execution_engine.py:85-111), timed as one prompt of
+    the mean length through 1 of the layers (the oracle's float32 prefill) and scaled by
+    the layers and prompts; decode: ``dec_steps`` batched steps of ``dec_batch`` rows at
+    the mean context ``dec_ctx``, each timed as 1 layer + 1/8 of the lm_head on torch CPU
+    (oracle/grpc_tp.py) and extrapolated.  Returns (seconds, description)."""
+    P = int(round(float(np.mean(prompt_lens)))) if len(prompt_lens) else 0
+    t_pre = cpu_prefill_sample(cfg, P, seed) * cfg.num_layers * len(prompt_lens) if P else 0.0
+    t_dec = 0.0
+    # the restated decode holds about 64 KB of float32 K/V copies per (row, context token):
+    # sample at most 131072 of them (about 8 GB) and scale by the rows
+    b_s = max(1, min(dec_batch, 131072 // max(1, dec_ctx)))
+    if dec_steps:
+        r = cpu_decode(cfg, 1, b_s, dec_ctx, 1, 1, seed, cpu_cores())
+        t_dec = statistics.median(r["step_s"]) * dec_steps * dec_batch / b_s
+    desc = (f"extrapolated from samples on this host's {cpu_cores()} cores: {len(prompt_lens)} prefills as one "
+            f"{P}-token prompt through 1 of {cfg.num_layers} layers (numpy float32) x prompts x layers, plus "
+            f"{dec_steps} decode steps of {dec_batch} rows at context {dec_ctx}, sampled as {b_s} rows through "
+            f"1 layer + 1/8 lm_head (torch CPU) x layers x {dec_batch}/{b_s}")
+    return t_pre + t_dec, desc
+
+
 def run_prefill(args):
     import torch
     import torch.distributed as dist
@@ -1349,6 +1373,15 @@ def run_mixed(args):
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                "api": "WorkerExecutionEngine.execute_step(StepRequest) with 16 prefill + 240 decode slots"}
 
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            t_cpu, desc = cpu_job_estimate(cfg, [MIXED_PROMPT] * MIXED_PREFILLS, MIXED_DECODES,
+                                           int(dec_ctx.mean()), 1, args.seed)
+            cpu = {"value": tokens / t_cpu, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
+                   "sample": desc}
+        except Exception as e:  # pragma: no cover - reported, not fatal
+            cpu = {"value": None, "unit": "tokens/s", "error": repr(e)}
     if rank == 0:
         line = {
             "metric": "mixed-step tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
@@ -1361,7 +1394,7 @@ def run_mixed(args):
                        "model": "mistral-7b-shape", "global_batch": MIXED_PREFILLS + MIXED_DECODES,
                        "seq_len": MIXED_PROMPT, "parallelism": f"tp{world}",
                        "l2": "inputs larger than L2 (weights + KV read per step >> 126 MB)"},
-            "e2e": e2e, "roofline": roofline, "cpu_baseline": None, "clocks": clk, "gpu_launches": launches,
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches,
             "parts_ms": {"prefill": ms_pre, "decode": ms_dec},
         }
         print(json.dumps(line), flush=True)
@@ -1550,6 +1583,14 @@ def run_tinyllama(args):
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                "api": "WorkerExecutionEngine.execute_step: 1 prefill step of 64 prompts + 127 decode steps"}
 
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            t_cpu, desc = cpu_job_estimate(cfg, lens.tolist(), B, int(lens.mean()) + TL_NEW // 2, TL_NEW - 1,
+                                           args.seed)
+            cpu = {"value": gen / t_cpu, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port", "sample": desc}
+        except Exception as e:  # pragma: no cover - reported, not fatal
+            cpu = {"value": None, "unit": "tokens/s", "error": repr(e)}
     if rank == 0:
         line = {
             "metric": "generated tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
@@ -1562,7 +1603,7 @@ def run_tinyllama(args):
                        "model": "tinyllama-1.1b-shape", "global_batch": B, "seq_len": TL_PROMPT[1] + TL_NEW,
                        "parallelism": f"tp{world}",
                        "l2": "inputs larger than L2 (2.2 GB of weights read per decode step)"},
-            "e2e": e2e, "roofline": roofline, "cpu_baseline": None, "clocks": clk, "gpu_launches": launches,
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches,
             "prompt_tokens_per_job": T_p,
         }
         print(json.dumps(line), flush=True)

@@ -69,3 +69,12 @@ def test_reference_arm_prefill_workload_prints_one_json_line():
     assert len(lines) == 1
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["metric"] == "prefill tokens/s" and d["value"] > 0
+
+
+def test_cpu_job_estimate_small_shape():
+    import bench
+    from pythonintern_b200 import workloads
+    cfg = workloads.tinyllama_config(num_layers=2)
+    cfg.vocab_size = 1024
+    t, desc = bench.cpu_job_estimate(cfg, [20, 36], 2, 64, 3, seed=0)
+    assert 0 < t < 120 and "2 prefills" in desc and "3 decode steps" in desc
