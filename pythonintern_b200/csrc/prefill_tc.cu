@@ -7,29 +7,35 @@
 // tokens at positions seq_ctx0[s] + (row - seq_start[s]); their K/V are already in the
 // paged pool (block-table row s).
 //
-// Work item = one kv head g and a tile of QT = 128 / REP consecutive tokens of one
-// sequence: its 128 MMA rows are the (token, query head) pairs that share g, row
-// m = token * REP + head, so every K/V tile serves QT tokens x REP heads.  The kernel is
-// persistent (one CTA per SM walking items w = blockIdx.x, + gridDim.x, ...).  Per CTA:
+// A Q tile is QT = 128 / REP consecutive tokens of one sequence for one kv head g: its 128
+// MMA rows are the (token, query head) pairs that share g, row m = token * REP + head, so
+// every K/V tile serves QT tokens x REP heads.  Work item = one kv head and a PAIR of
+// adjacent Q tiles of one sequence (the later tile in group 0, the one before it in group
+// 1), which read the same K/V tiles: each K/V tile brought into shared memory feeds two
+// S = Q K^T products.  The kernel is persistent (one CTA per SM walking items w =
+// blockIdx.x, + gridDim.x, ...).  Per CTA:
 //
-//   warp 0 / lane 0 : TMA producer.  Q per item (a 3D box [QT tokens][REP heads][64 dims],
-//                     twice for the two 64-dim halves, into one of two Q buffers, so the
-//                     next item's Q loads during this one), then per KV tile of 64 keys the
-//                     four 16-token pool blocks of K and of V (2D boxes [16 rows][64 dims]
-//                     through the block table) into a 3-stage ring; 128-byte swizzle, no
-//                     multicast.
-//   warp 1 / lane 0 : MMA issuer.  S(j) = Q K(j)^T (M=128, N=64, K=128) into one of two
-//                     TMEM S buffers; after S(j+1) is issued, PV(j) = P(j) V(j) (M=128,
-//                     N=128, K=64; V read in place, MN-major) into one of two TMEM PV
-//                     buffers.  tcgen05.commit signals each result and frees the K/V stage.
-//   warps 2-9       : two threads per MMA row (TMEM lane): warps w and w + 4 share a lane
-//                     quarter, each owning half of the row's 64 scores and 128 output dims.
-//                     Softmax of S(j) in the log2 domain with the causal mask (the two
-//                     halves exchange their row maxima through shared memory), P(j) to
-//                     shared memory in bf16 (the A operand of PV(j)), then
-//                     O = O * exp2(m_old - m_new) + PV(j-1) in registers; finally O / l.
+//   warp 0 / lane 0 : TMA producer.  Per item the two Q tiles (3D boxes [QT tokens][REP
+//                     heads][64 dims], two per tile for the 64-dim halves), then per K/V
+//                     tile of 64 keys the four 16-token pool blocks of K and of V (2D boxes
+//                     [16 rows][64 dims] through the block table) into a 3-stage ring;
+//                     128-byte swizzle, no multicast.
+//   warp 1 / lane 0 : MMA issuer.  Per K/V tile j: S_g(j) = Q_g K(j)^T (M=128, N=64, K=128)
+//                     for both groups into one of each group's two TMEM S buffers, then
+//                     O_g += P_g(j-1) V(j-1) (M=128, N=128, K=64; V read in place as an
+//                     MN-major operand) into each group's TMEM O accumulator.
+//   warps 2-5, 6-9  : softmax of group 0 and group 1, one thread per MMA row (TMEM lane):
+//                     the row's 64 scores of S(j) with the causal mask in the log2 domain,
+//                     P(j) in bf16 to one of the group's two shared-memory P tiles (the A
+//                     operand of its PV, so P(j + 1) is written while PV(j) runs), the
+//                     running sum of probabilities; at the end O / l from TMEM.
 //
-// S(j+1) and PV(j-1) run on the tensor cores while the threads work on S(j).  Every wait
+// O stays in TMEM.  P(j) is taken relative to the row's reference maximum m_ref, which
+// moves only when a tile's maximum exceeds it by more than 8 (a factor of 256): then the
+// warp rescales its rows of O in TMEM (after PV(j-1) has completed) and the running sum.
+// exp2(s - m_ref) <= 256 keeps P exact to bf16 and O, l in float32 range, and O / l does
+// not depend on the reference chosen, so the result is the softmax of the reference's
+// formula.  No barrier couples the warps: every hand-off is an mbarrier, and every wait
 // is bounded by %globaltimer; a timeout raises B2_DEV_PIPE_TIMEOUT and the CTA drains its
 // copies, frees TMEM and returns.  A block id outside the pool raises B2_DEV_RANGE and its
 // keys are read from block 0 and masked (so no uninitialised shared memory is ever used).
@@ -44,40 +50,27 @@ namespace pftc {
 
 using namespace b2::tc;
 
-// Named barrier over the softmax warps only (the producer and MMA warps keep running).
-__device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * 8) : "memory"); }
-// The same barrier, returning the AND of `pred` over all softmax threads, so that every
-// softmax warp leaves the main loop in the same iteration (a warp waiting at a named
-// barrier for a warp that already left would wait without bound).
-__device__ __forceinline__ bool softmax_all(bool pred) {
-  uint32_t out;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 1, %2, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(out)
-      : "r"((uint32_t)pred), "n"(32 * 8)
-      : "memory");
-  return out != 0;
-}
-
 constexpr int HD = 128;
-constexpr int ROWS = 128;                              // MMA M: (token, head) rows per CTA
+constexpr int ROWS = 128;                              // MMA M: (token, head) rows per Q tile
 constexpr int KT = 64;                                 // keys per KV tile (4 pool blocks)
 constexpr int ST = 3;                                  // KV ring stages
-constexpr int kSoftWarps = 8;                          // two per TMEM lane quarter: each owns half a row
-constexpr int kThreads = 64 + 32 * kSoftWarps;         // producer, MMA, softmax warps
+constexpr int NG = 2;                                  // Q tiles (softmax groups) per item
+constexpr int kGroupWarps = 4;                         // one per TMEM lane quarter
+constexpr int kThreads = 64 + 32 * NG * kGroupWarps;   // producer, MMA, softmax warps
 constexpr uint32_t HALF = KT * 64 * 2;                 // 8 KB: 64 keys x 64 dims
 constexpr uint32_t STAGE = 4 * HALF;                   // K lo | K hi | V lo | V hi
-constexpr uint32_t P_BYTES = ROWS * KT * 2;            // 16 KB
+constexpr uint32_t P_BYTES = ROWS * KT * 2;            // 16 KB: one P tile (two per group)
 constexpr uint32_t Q_HALF = ROWS * 64 * 2;             // 16 KB
-// Layout (1024-byte aligned): the K/V ring first, then P[2], then Q[2] (lo | hi each).
+constexpr uint32_t Q_BYTES = 2 * Q_HALF;               // one Q tile, lo | hi
+// Layout (1024-byte aligned): the K/V ring, then P[NG][2], then Q[NG]: 225 KB.
 constexpr uint32_t OFF_P = ST * STAGE;
-constexpr uint32_t OFF_Q = OFF_P + 2 * P_BYTES;
-constexpr size_t SMEM = OFF_Q + 4 * Q_HALF + 1024;
-constexpr uint32_t TMEM_COLS = 512;                    // S[2] (64 each) + PV[2] (128 each), rounded up
-constexpr uint32_t COL_S = 0, COL_PV = 128;
+constexpr uint32_t OFF_Q = OFF_P + NG * 2 * P_BYTES;
+constexpr size_t SMEM = OFF_Q + NG * Q_BYTES + 1024;
+static_assert(SMEM + 512 <= 232448, "shared memory above the 227 KB a CTA may use");
+// TMEM per group (256 columns): S[2] (64 each) then O (128); 512 in all.
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t GROUP_COLS = 256, COL_S = 0, COL_O = 128;
+constexpr float kRescale = 8.f;                        // log2 of the largest P before O is rescaled
 
 struct Params {
   int n_rows, nq, nkv;
@@ -106,46 +99,68 @@ __device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t addr, uint32_t l
   return d;
 }
 
-// One work item: a tile of QT tokens of one sequence, for one kv head.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 32 lanes x 32 consecutive 32-bit columns stored to TMEM (the caller waits with
+// tmem_wait_st() before the tensor cores may read them).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// One work item: kv head g and up to two Q tiles of one sequence (tile 1 may be empty).
 struct Item {
-  int rs, t0, nt, ctx0, n_kv, g;
+  int rs, ctx0, g;
+  int t0[NG], nt[NG], n_kv[NG];
   const int32_t* table;
   bool valid;
 };
 
-// Tiles of QT tokens over all sequences (every lane of the calling warp gets the total).
-__device__ __forceinline__ int count_tiles(const Params& p, int qt, int lane) {
+// Q-tile pairs of QT tokens over all sequences (every lane of the calling warp gets the total).
+__device__ __forceinline__ int count_pairs(const Params& p, int qt, int lane) {
   int total = 0;
   for (int s0 = 0; s0 < p.n_seqs; s0 += 32) {
     const int s = s0 + lane;
-    int nt = 0;
+    int np = 0;
     if (s < p.n_seqs) {
       const int len = p.seq_start[s + 1] - p.seq_start[s];
-      nt = len > 0 ? (len + qt - 1) / qt : 0;
+      np = len > 0 ? ((len + qt - 1) / qt + 1) / 2 : 0;
     }
-    total += __reduce_add_sync(0xffffffffu, nt);
+    total += __reduce_add_sync(0xffffffffu, np);
   }
   return total;
 }
 
-// Item w: kv head w % nkv of tile w / nkv, tiles numbered sequence by sequence with each
-// sequence's last (longest) tile first.  Every warp computes the same answer (warp prefix
-// sums over the sequences); all lanes of the calling warp take part.
+// Item w: kv head w % nkv of pair w / nkv, pairs numbered sequence by sequence with each
+// sequence's last (longest) tiles first: pair u holds tiles 2u and 2u + 1 counted from the
+// end of the sequence.  Every warp computes the same answer (warp prefix sums over the
+// sequences); all lanes of the calling warp take part.
 template <int QT>
 __device__ Item find_item(const Params& p, int w, int lane) {
   Item it{};
   it.valid = false;
   const int bx = w / p.nkv;
   it.g = w % p.nkv;
-  int seq = -1, tile = 0, base = 0;
+  int seq = -1, pair = 0, base = 0;
   for (int s0 = 0; s0 < p.n_seqs && seq < 0; s0 += 32) {
     const int s = s0 + lane;
-    int nt = 0;
+    int np = 0;
     if (s < p.n_seqs) {
       const int len = p.seq_start[s + 1] - p.seq_start[s];
-      nt = len > 0 ? (len + QT - 1) / QT : 0;
+      np = len > 0 ? ((len + QT - 1) / QT + 1) / 2 : 0;
     }
-    int inc = nt;
+    int inc = np;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int v = __shfl_up_sync(0xffffffffu, inc, o);
@@ -157,9 +172,9 @@ __device__ Item find_item(const Params& p, int w, int lane) {
       const unsigned hit = __ballot_sync(0xffffffffu, b < inc);
       const int l = __ffs(hit) - 1;
       const int inc_l = __shfl_sync(0xffffffffu, inc, l);
-      const int nt_l = __shfl_sync(0xffffffffu, nt, l);
+      const int np_l = __shfl_sync(0xffffffffu, np, l);
       seq = s0 + l;
-      tile = b - (inc_l - nt_l);
+      pair = b - (inc_l - np_l);
     }
     base += total;
   }
@@ -172,56 +187,64 @@ __device__ Item find_item(const Params& p, int w, int lane) {
   }
   const int len = re - rs;
   const int ntile = (len + QT - 1) / QT;
+#pragma unroll
+  for (int q = 0; q < NG; ++q) {
+    const int tile = 2 * pair + q;  // counted from the end of the sequence
+    if (tile < ntile) {
+      it.t0[q] = (ntile - 1 - tile) * QT;          // first token of the tile within its sequence
+      it.nt[q] = min(QT, len - it.t0[q]);          // tokens in the tile (>= 1)
+      it.n_kv[q] = (ctx0 + it.t0[q] + it.nt[q] - 1) / KT + 1;  // KV tiles up to its last position
+    } else {
+      it.t0[q] = 0;
+      it.nt[q] = 0;
+      it.n_kv[q] = 0;
+    }
+  }
   it.rs = rs;
-  it.t0 = (ntile - 1 - tile) * QT;  // first token of the tile within its sequence
-  it.nt = min(QT, len - it.t0);     // tokens in the tile (>= 1)
   it.ctx0 = ctx0;
-  it.n_kv = (ctx0 + it.t0 + it.nt - 1) / KT + 1;  // KV tiles of 64 keys up to the last position
   it.table = p.tables + (int64_t)seq * p.table_stride;
   it.valid = true;
   return it;
 }
 
-// Persistent: one CTA per SM walks the items w = blockIdx.x, + gridDim.x, ...; barriers,
-// TMEM and the rings are set up once, the producer prefetches the next item's Q into the
-// second Q buffer, and tile counters (ring stages, S/PV buffers, barrier phases) run on
-// across items.
 template <int REP>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const Params p) {
   constexpr int QT = ROWS / REP;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full[2];
-  __shared__ __align__(8) uint64_t q_empty[2];
+  __shared__ __align__(8) uint64_t q_full[NG];
+  __shared__ __align__(8) uint64_t q_empty[NG];
   __shared__ __align__(8) uint64_t kv_full[ST];
   __shared__ __align__(8) uint64_t kv_empty[ST];
-  __shared__ __align__(8) uint64_t s_full[2];
-  __shared__ __align__(8) uint64_t s_empty[2];
-  __shared__ __align__(8) uint64_t p_full[2];
-  __shared__ __align__(8) uint64_t pv_full[2];
-  __shared__ __align__(8) uint64_t pv_empty[2];
+  __shared__ __align__(8) uint64_t s_full[NG][2];
+  __shared__ __align__(8) uint64_t s_empty[NG][2];
+  __shared__ __align__(8) uint64_t p_full[NG][2];
+  __shared__ __align__(8) uint64_t pv_done[NG][2];
+  __shared__ __align__(8) uint64_t o_empty[NG];
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
-  __shared__ float s_red[2][2][ROWS];  // [tile parity][half][row]: the halves' row maxima
-  __shared__ float s_l[2][ROWS];       // [half][row]: the halves' final sums of probabilities
 
   pdl_wait();  // the metadata, q and the pool may come from the preceding kernels
   pdl_trigger();
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_items = count_tiles(p, QT, lane) * p.nkv;
+  const int n_items = count_pairs(p, QT, lane) * p.nkv;
   if ((int)blockIdx.x >= n_items) return;  // nothing allocated yet
 
   if (threadIdx.x == 0) {
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&q_full[b], 1);
-      mbar_init(&q_empty[b], 1);
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], kSoftWarps);
-      mbar_init(&p_full[b], kSoftWarps);
-      mbar_init(&pv_full[b], 1);
-      mbar_init(&pv_empty[b], kSoftWarps);
+    for (int g = 0; g < NG; ++g) {
+      mbar_init(&q_full[g], 1);
+      mbar_init(&q_empty[g], 1);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&s_full[g][b], 1);
+        mbar_init(&s_empty[g][b], kGroupWarps);
+      }
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&p_full[g][b], kGroupWarps);
+        mbar_init(&pv_done[g][b], 1);
+      }
+      mbar_init(&o_empty[g], kGroupWarps);
     }
     for (int s = 0; s < ST; ++s) {
       mbar_init(&kv_full[s], 1);
@@ -243,58 +266,75 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- TMA producer
     const uint64_t pol_q = policy_evict_first();
     const uint64_t pol_kv = policy_evict_last();  // K/V tiles are re-read by the sequence's other tiles
-    int i = 0, J = 0;
+    int iq[NG] = {0, 0};  // Q loads into each group's buffer
+    int J = 0;            // K/V tiles through the ring
     bool ok = true;
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
       const Item it = find_item<QT>(p, w, lane);
       if (!it.valid) continue;
       if (lane == 0) {
-        const int qb = i & 1;
-        if (!mbar_wait(&q_empty[qb], ((uint32_t)(i >> 1) & 1u) ^ 1u)) {
-          raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
-          ok = false;
-        } else {
-          uint8_t* qs = smem + OFF_Q + qb * 2 * Q_HALF;
-          mbar_arrive_expect_tx(&q_full[qb], 2 * Q_HALF);
-          tma_load_3d(qs, &tmQ, &q_full[qb], 0, it.g * REP, it.rs + it.t0, pol_q);
-          tma_load_3d(qs + Q_HALF, &tmQ, &q_full[qb], 64, it.g * REP, it.rs + it.t0, pol_q);
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          if (it.nt[g] == 0 || !ok) continue;
+          if (!mbar_wait(&q_empty[g], ((uint32_t)iq[g] & 1u) ^ 1u)) {
+            raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+            ok = false;
+            continue;
+          }
+          uint8_t* qs = smem + OFF_Q + g * Q_BYTES;
+          mbar_arrive_expect_tx(&q_full[g], Q_BYTES);
+          tma_load_3d(qs, &tmQ, &q_full[g], 0, it.g * REP, it.rs + it.t0[g], pol_q);
+          tma_load_3d(qs + Q_HALF, &tmQ, &q_full[g], 64, it.g * REP, it.rs + it.t0[g], pol_q);
+          ++iq[g];
         }
-        const int last_pos = it.ctx0 + it.t0 + it.nt - 1;
-        for (int j = 0; j < it.n_kv && ok; ++j, ++J) {
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      // Lane b < 4 reads the pool block of key block 4 j + b of the next K/V tile while lane 0
+      // waits for a ring stage and issues the current tile's copies.
+      const int last_pos = it.ctx0 + it.t0[0] + it.nt[0] - 1;  // tile 0 is the later one
+      auto block_of = [&](int j) -> int {
+        if (lane >= KT / 16) return 0;
+        const int bi = j * (KT / 16) + lane;
+        const int blk = bi < p.table_stride ? it.table[bi] : -1;
+        if (blk < 0 || blk >= p.num_blocks) {
+          // A block holding keys some row attends to must exist; past the last position
+          // the keys are masked and any valid block serves as filler.
+          if (bi * 16 <= last_pos) raise_status(p.status, B2_DEV_RANGE);
+          return 0;
+        }
+        return blk;
+      };
+      int blk_next = block_of(0);
+      for (int j = 0; j < it.n_kv[0] && ok; ++j, ++J) {
+        const int blk_cur = blk_next;
+        if (j + 1 < it.n_kv[0]) blk_next = block_of(j + 1);
+        int y[KT / 16];
+#pragma unroll
+        for (int b = 0; b < KT / 16; ++b) y[b] = __shfl_sync(0xffffffffu, blk_cur, b) * 16;
+        if (lane == 0) {
           const int st = J % ST;
           if (!mbar_wait(&kv_empty[st], ((uint32_t)(J / ST) & 1u) ^ 1u)) {
             raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
             ok = false;
-            break;
-          }
-          uint8_t* sb = smem + (size_t)st * STAGE;
-          mbar_arrive_expect_tx(&kv_full[st], STAGE);
-          for (int b = 0; b < KT / 16; ++b) {
-            const int bi = j * (KT / 16) + b;
-            int blk = bi < p.table_stride ? it.table[bi] : -1;
-            if (blk < 0 || blk >= p.num_blocks) {
-              // A block holding keys some row attends to must exist; past the last position
-              // the keys are masked and any valid block serves as filler.
-              if (bi * 16 <= last_pos) raise_status(p.status, B2_DEV_RANGE);
-              blk = 0;
+          } else {
+            uint8_t* sb = smem + (size_t)st * STAGE;
+            mbar_arrive_expect_tx(&kv_full[st], STAGE);
+#pragma unroll
+            for (int b = 0; b < KT / 16; ++b) {
+              tma_load_2d(sb + b * 2048, &tmK, &kv_full[st], it.g * HD, y[b], pol_kv);
+              tma_load_2d(sb + HALF + b * 2048, &tmK, &kv_full[st], it.g * HD + 64, y[b], pol_kv);
+              tma_load_2d(sb + 2 * HALF + b * 2048, &tmV, &kv_full[st], it.g * HD, y[b], pol_kv);
+              tma_load_2d(sb + 3 * HALF + b * 2048, &tmV, &kv_full[st], it.g * HD + 64, y[b], pol_kv);
             }
-            const int y = blk * 16;
-            tma_load_2d(sb + b * 2048, &tmK, &kv_full[st], it.g * HD, y, pol_kv);
-            tma_load_2d(sb + HALF + b * 2048, &tmK, &kv_full[st], it.g * HD + 64, y, pol_kv);
-            tma_load_2d(sb + 2 * HALF + b * 2048, &tmV, &kv_full[st], it.g * HD, y, pol_kv);
-            tma_load_2d(sb + 3 * HALF + b * 2048, &tmV, &kv_full[st], it.g * HD + 64, y, pol_kv);
           }
         }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
       }
-      ++i;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
     }
     if (lane == 0) {
       // Copies still in flight (only after an aborted pipeline) land before the CTA exits.
-      for (int q = 0; q < 2 && q < i; ++q) {
-        const int last_q = q + ((i - 1 - q) / 2) * 2;
-        mbar_wait(&q_full[q], (uint32_t)(last_q >> 1) & 1u, 100000000ull);
-      }
+      for (int g = 0; g < NG; ++g)
+        if (iq[g] > 0) mbar_wait(&q_full[g], (uint32_t)(iq[g] - 1) & 1u, 100000000ull);
       for (int st = 0; st < ST && st < J; ++st) {
         const int last_i = st + ((J - 1 - st) / ST) * ST;
         mbar_wait(&kv_full[st], (uint32_t)(last_i / ST) & 1u, 100000000ull);
@@ -305,62 +345,86 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer
     constexpr uint32_t idesc_s = instr_desc_bf16(ROWS, KT);
     constexpr uint32_t idesc_pv = instr_desc_bf16(ROWS, HD) | (1u << 16);  // B (V) MN-major
-    int i = 0, J = 0;
+    int iq[NG] = {0, 0};  // Q tiles consumed per group
+    int js[NG] = {0, 0};  // S tiles issued per group (= PV tiles issued, after each item)
+    int jp[NG] = {0, 0};  // PV tiles issued per group
+    int io[NG] = {0, 0};  // items started per group (O hand-offs)
+    int J = 0;
     bool ok = true;
-    auto issue_pv = [&](int Jx) -> bool {  // PV of global tile Jx
-      const int b = Jx & 1;
-      if (!mbar_wait(&p_full[b], (uint32_t)(Jx >> 1) & 1u) ||
-          !mbar_wait(&pv_empty[b], ((uint32_t)(Jx >> 1) & 1u) ^ 1u)) {
-        raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
-        return false;
+    // O_g (+)= P_g V of the K/V tile in ring stage `st`; `first` starts the item's O.
+    auto issue_pv = [&](int g, int st, bool first) -> bool {
+      const int pb = jp[g] & 1;
+      if (!mbar_wait(&p_full[g][pb], (uint32_t)(jp[g] >> 1) & 1u)) return false;
+      if (first) {  // the previous item's O has been read out of TMEM
+        if (!mbar_wait(&o_empty[g], ((uint32_t)io[g] & 1u) ^ 1u)) return false;
+        ++io[g];
       }
       tc_fence_after();
-      const uint32_t p_addr = smem_u32(smem + OFF_P + b * P_BYTES);
-      const uint32_t v_addr = smem_u32(smem + (size_t)(Jx % ST) * STAGE + 2 * HALF);
+      const uint32_t p_addr = smem_u32(smem + OFF_P + (g * 2 + pb) * P_BYTES);
+      const uint32_t v_addr = smem_u32(smem + (size_t)st * STAGE + 2 * HALF);
 #pragma unroll
       for (int kk = 0; kk < KT / 16; ++kk)  // 16 keys per MMA: +32 bytes of P rows, +2 KB of V rows
-        umma_bf16(tmem + COL_PV + b * HD, smem_desc_sw128(p_addr) + 2 * kk,
-                  smem_desc_sw128_mn(v_addr + kk * 2048, HALF, 1024), idesc_pv, kk > 0 ? 1u : 0u);
-      umma_commit(&pv_full[b]);
-      umma_commit(&kv_empty[Jx % ST]);
+        umma_bf16(tmem + g * GROUP_COLS + COL_O, smem_desc_sw128(p_addr) + 2 * kk,
+                  smem_desc_sw128_mn(v_addr + kk * 2048, HALF, 1024), idesc_pv, (first && kk == 0) ? 0u : 1u);
+      umma_commit(&pv_done[g][pb]);
+      ++jp[g];
       return true;
     };
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
       const Item it = find_item<QT>(p, w, lane);
       if (!it.valid) continue;
       if (lane == 0) {
-        const int qb = i & 1;
-        if (!mbar_wait(&q_full[qb], (uint32_t)(i >> 1) & 1u)) {
-          raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
-          ok = false;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          if (it.nt[g] == 0 || !ok) continue;
+          if (!mbar_wait(&q_full[g], (uint32_t)iq[g] & 1u)) ok = false;
+          ++iq[g];
         }
-        const uint32_t q_addr = smem_u32(smem + OFF_Q + qb * 2 * Q_HALF);
-        for (int j = 0; j < it.n_kv && ok; ++j, ++J) {
-          const int st = J % ST, b = J & 1;
-          if (!mbar_wait(&kv_full[st], (uint32_t)(J / ST) & 1u) ||
-              !mbar_wait(&s_empty[b], ((uint32_t)(J >> 1) & 1u) ^ 1u)) {
-            raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+        for (int j = 0; j < it.n_kv[0] && ok; ++j, ++J) {
+          const int st = J % ST;
+          if (!mbar_wait(&kv_full[st], (uint32_t)(J / ST) & 1u)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t k_addr = smem_u32(smem + (size_t)st * STAGE);
 #pragma unroll
-          for (int half = 0; half < 2; ++half)
+          for (int g = 0; g < NG; ++g) {
+            if (j >= it.n_kv[g] || !ok) continue;
+            const int b = js[g] & 1;
+            if (!mbar_wait(&s_empty[g][b], ((uint32_t)(js[g] >> 1) & 1u) ^ 1u)) {
+              ok = false;
+              continue;
+            }
+            tc_fence_after();
+            const uint32_t q_addr = smem_u32(smem + OFF_Q + g * Q_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16(tmem + COL_S + b * KT, smem_desc_sw128(q_addr + half * Q_HALF) + 2 * kk,
-                        smem_desc_sw128(k_addr + half * HALF) + 2 * kk, idesc_s, (half | kk) ? 1u : 0u);
-          umma_commit(&s_full[b]);
-          if (j >= 1 && !issue_pv(J - 1)) {
-            ok = false;
-            break;
+            for (int half = 0; half < 2; ++half)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                umma_bf16(tmem + g * GROUP_COLS + COL_S + b * KT, smem_desc_sw128(q_addr + half * Q_HALF) + 2 * kk,
+                          smem_desc_sw128(k_addr + half * HALF) + 2 * kk, idesc_s, (half | kk) ? 1u : 0u);
+            umma_commit(&s_full[g][b]);
+            ++js[g];
+            if (j == it.n_kv[g] - 1) umma_commit(&q_empty[g]);  // every S MMA of this tile has read Q_g
+          }
+          if (j >= 1) {
+            const int pst = (J - 1) % ST;
+#pragma unroll
+            for (int g = 0; g < NG; ++g)
+              if (ok && j - 1 < it.n_kv[g]) ok = issue_pv(g, pst, j == 1);
+            umma_commit(&kv_empty[pst]);  // both groups' S and PV of tile j - 1 have been issued
           }
         }
-        if (ok) ok = issue_pv(J - 1);  // the item's last tile
-        umma_commit(&q_empty[qb]);     // every S MMA of this item has read Q buffer qb
+        if (ok && it.n_kv[0] > 0) {  // the item's last tile
+          const int pst = (J - 1) % ST;
+#pragma unroll
+          for (int g = 0; g < NG; ++g)
+            if (ok && it.n_kv[g] == it.n_kv[0]) ok = issue_pv(g, pst, it.n_kv[0] == 1);
+          umma_commit(&kv_empty[pst]);
+        }
+        if (!ok) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
       }
-      ++i;
       ok = __shfl_sync(0xffffffffu, ok, 0);
     }
     if (lane == 0) {
@@ -369,143 +433,151 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- softmax / accumulation: two threads per MMA row
+    // ---------------- softmax: one thread per MMA row of its group's Q tile
     const int sw = warp - 2;                 // 0..7
+    const int grp = sw / kGroupWarps;        // 0: the later Q tile, 1: the one before
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
-    const int half = sw >> 2;                // which half of the row's scores and dims
     const int m = quarter * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + grp * GROUP_COLS;
     const int tk = m / REP, h = m % REP;
-    int J = 0;
+    int js = 0;  // S tiles consumed by this group (the PV of tile js - 1 is the latest issued)
     bool ok = true;
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
       const Item it = find_item<QT>(p, w, lane);
-      if (!it.valid) continue;
-      const bool row_ok = tk < it.nt;
-      const int pos = it.ctx0 + it.t0 + tk;  // this row's token position (the last key it attends to)
-      float o[HD / 2];
-#pragma unroll
-      for (int c = 0; c < HD / 2; ++c) o[c] = 0.f;
-      float m_run = -INFINITY, l_run = 0.f, m_o = -INFINITY;
-      float m_tile[2] = {-INFINITY, -INFINITY};
-      auto accumulate = [&](int Jx) {  // O = O * exp2(m_o - m(Jx)) + PV(Jx), this thread's 64 dims
-        const int b = Jx & 1;
-        // warp-uniform verdict: the TMEM loads below are .sync.aligned
-        const bool done = __all_sync(0xffffffffu, mbar_wait(&pv_full[b], (uint32_t)(Jx >> 1) & 1u));
-        if (!done) {
-          if (lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+      // this group's tile (selected without indexing, so the item stays in registers)
+      const int nt = grp ? it.nt[1] : it.nt[0];
+      const int t0 = grp ? it.t0[1] : it.t0[0];
+      const int n_kv = grp ? it.n_kv[1] : it.n_kv[0];
+      if (!it.valid || nt == 0) continue;
+      const bool row_ok = tk < nt;
+      const int pos = it.ctx0 + t0 + tk;  // this row's token position (the last key it attends to)
+      float m_ref = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < n_kv; ++j, ++js) {
+        const int b = js & 1;
+        // warp-uniform verdicts: the TMEM loads and stores below are .sync.aligned
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[grp][b], (uint32_t)(js >> 1) & 1u))) {
           ok = false;
+          break;
         }
         tc_fence_after();
-        uint32_t r0[32], r1[32];
-        const uint32_t a = tmem + lane_off + COL_PV + b * HD + half * (HD / 2);
-        tmem_ld32_nowait(a, r0);
-        tmem_ld32_nowait(a + 32, r1);
+        uint32_t sr[64];
+        tmem_ld32_nowait(trow + COL_S + b * KT, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tmem_ld32_nowait(trow + COL_S + b * KT + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
         tmem_wait_ld();
-        const float mi = m_tile[b];
-        const float corr = (m_o == -INFINITY) ? 0.f : exp2f(m_o - mi);
-        if (done) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            o[e] = o[e] * corr + __uint_as_float(r0[e]);
-            o[32 + e] = o[32 + e] * corr + __uint_as_float(r1[e]);
-          }
-          m_o = mi;
-        }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&pv_empty[b]);
-      };
-      for (int j = 0; j < it.n_kv; ++j, ++J) {
-        const int b = J & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (uint32_t)(J >> 1) & 1u))) {
-          if (lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
-          ok = false;
-        }
-        // both halves of every row meet at the exchange below, so a failed wait still runs
-        // the barrier (with nothing valid) before every softmax warp leaves the loop
-        tc_fence_after();
-        uint32_t sr[32];
-        tmem_ld32_nowait(tmem + lane_off + COL_S + b * KT + half * 32, sr);
-        tmem_wait_ld();
-        const int k0 = j * KT + half * 32;
-        float sv[32];
-        float mx = -INFINITY;
-        if (ok && row_ok && k0 + 31 <= pos) {  // every key of this half-tile is visible (the common case)
+        if (lane == 0) mbar_arrive(&s_empty[grp][b]);  // the S buffer may be rewritten
+        // raw scores; masked keys are -inf (scale_log2 > 0, so the maximum commutes with it)
+        const int k0 = j * KT;
+        float sv[64];
+        if (row_ok && k0 + KT - 1 <= pos) {  // every key of the tile is visible (the common case)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            sv[e] = __uint_as_float(sr[e]) * p.scale_log2;
-            mx = fmaxf(mx, sv[e]);
-          }
+          for (int e = 0; e < 64; ++e) sv[e] = __uint_as_float(sr[e]);
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const bool valid = ok && row_ok && k0 + e <= pos;
-            sv[e] = valid ? __uint_as_float(sr[e]) * p.scale_log2 : -INFINITY;
-            mx = fmaxf(mx, sv[e]);
+          for (int e = 0; e < 64; ++e) sv[e] = (row_ok && k0 + e <= pos) ? __uint_as_float(sr[e]) : -INFINITY;
+        }
+        float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+        for (int e = 4; e < 64; e += 4)
+#pragma unroll
+          for (int u = 0; u < 4; ++u) mx4[u] = fmaxf(mx4[u], sv[e + u]);
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
+        // the reference maximum: set by the first visible key, raised only by more than kRescale
+        bool need = false;
+        float corr = 1.f;
+        if (m_ref == -INFINITY) {
+          m_ref = mx;
+        } else if (mx > m_ref + kRescale) {
+          need = true;
+          corr = exp2f(m_ref - mx);
+        }
+        // P buffer b was last read by PV(js - 2), normally long complete
+        if (js >= 2 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[grp][b], (uint32_t)((js - 2) >> 1) & 1u))) {
+          ok = false;
+          break;
+        }
+        if (__any_sync(0xffffffffu, need)) {
+          // O must hold PV(js - 1) before it is rescaled (need implies j >= 1)
+          if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[grp][(js - 1) & 1], (uint32_t)((js - 1) >> 1) & 1u))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < HD; c += 32) {
+            uint32_t o[32];
+            tmem_ld32_nowait(trow + COL_O + c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+            tmem_st32(trow + COL_O + c, o);
+          }
+          tmem_wait_st();
+          if (need) {
+            l_run *= corr;
+            m_ref = mx;
           }
         }
-        s_red[J & 1][half][m] = mx;
-        ok = softmax_all(ok);
-        mx = fmaxf(mx, s_red[J & 1][half ^ 1][m]);
-        if (!ok) break;
-        const float m_new = fmaxf(m_run, mx);
-        // P = exp2(s - m_new) in bf16 into this half's four 16-byte chunks of the swizzled row
-        uint8_t* prow = smem + OFF_P + b * P_BYTES + m * 128;
-        float lsum = 0.f;
-        // a row with nothing visible yet keeps p = 0 (exp2(-inf - -inf) would be NaN)
-        const float m_sub = m_new == -INFINITY ? 0.f : m_new;
+        // P = exp2(s * scale_log2 - m_ref) in bf16 into the swizzled row of the group's P tile;
+        // a row with nothing visible keeps p = 0 (m_ref = -inf is replaced by 0)
+        const float m_sub = m_ref == -INFINITY ? 0.f : m_ref;
+        uint8_t* prow = smem + OFF_P + (grp * 2 + b) * P_BYTES + m * 128;
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 8; ++q) {
           uint32_t wv[4];
 #pragma unroll
           for (int e2 = 0; e2 < 4; ++e2) {
             const int e = q * 8 + e2 * 2;
-            const float p0 = exp2f(sv[e] - m_sub);  // sv = -inf (masked) gives 0
-            const float p1 = exp2f(sv[e + 1] - m_sub);
-            lsum += p0 + p1;
+            const float p0 = ex2_approx(fmaf(sv[e], p.scale_log2, -m_sub));  // -inf gives 0
+            const float p1 = ex2_approx(fmaf(sv[e + 1], p.scale_log2, -m_sub));
+            ls[e2] += p0 + p1;
             __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
             wv[e2] = *reinterpret_cast<uint32_t*>(&h2);
           }
-          const int chunk = half * 4 + q;
-          *reinterpret_cast<uint4*>(prow + ((chunk ^ (m & 7)) << 4)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          *reinterpret_cast<uint4*>(prow + ((q ^ (m & 7)) << 4)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
-        l_run = (m_run == -INFINITY ? 0.f : l_run * exp2f(m_run - m_new)) + lsum;
-        m_run = m_new;
-        m_tile[b] = m_new;
-        fence_proxy_async_smem();  // P[b] written by these threads is read by the tensor cores
-        tc_fence_before();
+        l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        fence_proxy_async_smem();  // P written by these threads is read by the tensor cores
+        tc_fence_before();         // and so are the rescaled O columns
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&s_empty[b]);
-          mbar_arrive(&p_full[b]);
-        }
-        if (j >= 1) accumulate(J - 1);
+        if (lane == 0) mbar_arrive(&p_full[grp][b]);
       }
-      // No early exit here: a failed wait inside accumulate() is per warp, and every softmax
-      // warp must reach the exchange below, which makes the verdict uniform again.
-      if (ok) accumulate(J - 1);  // the item's last tile
-      // the row's sum of probabilities is the sum of the two halves' (same running maximum)
-      s_l[half][m] = l_run;
-      ok = softmax_all(ok);
-      const float l_tot = l_run + s_l[half ^ 1][m];
-      // O / l to global memory: this thread's 64 dims of the row, 16-byte stores
-      if (ok && row_ok) {
-        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)(it.rs + it.t0 + tk) * p.ld_out +
-                             (int64_t)(it.g * REP + h) * HD + half * (HD / 2);
+      if (!ok) break;
+      // O / l to global memory once the item's last PV has completed; then O may be reused
+      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[grp][(js - 1) & 1], (uint32_t)((js - 1) >> 1) & 1u))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) +
+                           (int64_t)(it.rs + t0 + tk) * p.ld_out + (int64_t)(it.g * REP + h) * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t o[32];
+        tmem_ld32_nowait(trow + COL_O + c, o);
+        tmem_wait_ld();
+        if (row_ok) {
 #pragma unroll
-        for (int c = 0; c < HD / 2; c += 8) {
-          uint32_t wv[4];
+          for (int u = 0; u < 32; u += 8) {
+            uint32_t wv[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(o[c + 2 * u] * inv, o[c + 2 * u + 1] * inv);
-            wv[u] = *reinterpret_cast<uint32_t*>(&h2);
+            for (int e = 0; e < 4; ++e) {
+              __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(o[u + 2 * e]) * inv,
+                                                        __uint_as_float(o[u + 2 * e + 1]) * inv);
+              wv[e] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            *reinterpret_cast<uint4*>(dst + c + u) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
           }
-          *reinterpret_cast<uint4*>(dst + c) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[grp]);
     }
+    if (!ok && lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
   }
 
   // ---------------- teardown
@@ -589,7 +661,7 @@ int prefill_attention_tc(const void* q, int64_t ld_q, int n_rows, int nq, int nk
     rc = encode(&mv, vb, 2, dims, strides, box);
     if (rc) return rc;
   }
-  const long items = (long)(n_rows / qt + n_seqs) * nkv;  // an upper bound; the kernel counts exactly
+  const long items = (long)((n_rows / qt + n_seqs) / 2 + n_seqs) * nkv;  // an upper bound; the kernel counts exactly
   const dim3 grid((unsigned)(items < sm_count() ? items : sm_count()));
   auto go = [&](void (*k)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const Params)) -> int {
     const int rc = allow_smem_once((const void*)k, SMEM);

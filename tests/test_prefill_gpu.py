@@ -147,6 +147,35 @@ def test_prefill_attention_tensor_cores_vs_oracle(nq, nkv, lens, ctx0):
     assert torch.equal(out, _run(q, kc, vc, tab, lens, ctx0, nq, nkv, hd))
 
 
+@pytest.mark.parametrize("nq,nkv", [(32, 8), (8, 1)])
+def test_prefill_attention_tensor_cores_rising_scores(nq, nkv):
+    """Scores that climb by about 8.7 (log2 units) from one 64-key tile to the next, so the
+    kernel's running reference maximum moves on every tile and O is rescaled in TMEM; and
+    falling scores, where it never moves and P stays far below 1."""
+    hd = 128
+    lens, ctx0 = [300, 517], [0, 70]
+    for sign in (1.0, -1.0):
+        q, kc, vc, tables, tab = _case(lens, ctx0, nq, nkv, hd, seed=nq + 41)
+        gen = torch.Generator().manual_seed(5)
+        q = (1.0 + 0.05 * torch.randn(q.shape, generator=gen)).to(torch.bfloat16)
+        # the key at position t of every sequence: score ~ sign * 6 * (t // 64) + noise
+        for s, tb in enumerate(tables):
+            for t in range(ctx0[s] + lens[s]):
+                blk, off = tb[t // 16], t % 16
+                a = sign * 6.0 * (t // 64) / (hd / math.sqrt(hd))
+                kc[0, blk, off] = (a + 0.02 * torch.randn(nkv, hd, generator=gen)).to(torch.bfloat16)
+        out = _run_tc(q, kc, vc, tab, lens, ctx0, nq, nkv, hd)
+        torch.cuda.synchronize()
+        _lib.check_device_status(DEV, "prefill attention (tensor cores, rescaling)")
+        rows = sorted({0, 1, 63, 64, 65, 128, 200, 299, 300, 301, 400, 555, 700, 816})
+        want = _oracle_rows_subset(q, kc, vc, tables, lens, ctx0, rows)
+        got = to_np(out)[rows]
+        assert np.isfinite(got).all()
+        assert rel(got, want) < 1e-2, sign
+        for i, r in enumerate(rows):
+            assert rel(got[i], want[i]) < 3e-2, (sign, r)
+
+
 def _oracle_rows_subset(q, kc, vc, tables, lens, ctx0, rows):
     T, nq, hd = q.shape
     nkv = kc.shape[3]
