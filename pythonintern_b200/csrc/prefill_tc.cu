@@ -22,21 +22,22 @@
 //                     128-byte swizzle, no multicast.
 //   warp 1 / lane 0 : MMA issuer.  Per K/V tile j: S_g(j) = Q_g K(j)^T (M=128, N=64, K=128)
 //                     for both groups into one of each group's two TMEM S buffers, then
-//                     O_g += P_g(j-1) V(j-1) (M=128, N=128, K=64; V read in place as an
-//                     MN-major operand) into each group's TMEM O accumulator.
+//                     O_g += P_g(j-1) V(j-1) (M=128, N=128, K=64; P read from TMEM, V in
+//                     place from shared memory as an MN-major operand) into each group's
+//                     TMEM O accumulator.
 //   warps 2-5, 6-9  : softmax of group 0 and group 1, one thread per MMA row (TMEM lane):
 //                     the row's 64 scores of S(j) with the causal mask in the log2 domain,
-//                     P(j) in bf16 to one of the group's two shared-memory P tiles (the A
-//                     operand of its PV, so P(j + 1) is written while PV(j) runs), the
-//                     running sum of probabilities; at the end O / l from TMEM.
+//                     P(j) in bf16 back into TMEM over the S(j) it was computed from (the A
+//                     operand of PV(j)), the running sum of probabilities; at the end O / l.
 //
 // O stays in TMEM.  P(j) is taken relative to the row's reference maximum m_ref, which
 // moves only when a tile's maximum exceeds it by more than 8 (a factor of 256): then the
 // warp rescales its rows of O in TMEM (after PV(j-1) has completed) and the running sum.
 // exp2(s - m_ref) <= 256 keeps P exact to bf16 and O, l in float32 range, and O / l does
 // not depend on the reference chosen, so the result is the softmax of the reference's
-// formula.  No barrier couples the warps: every hand-off is an mbarrier, and every wait
-// is bounded by %globaltimer; a timeout raises B2_DEV_PIPE_TIMEOUT and the CTA drains its
+// formula.  No barrier couples the warps: every hand-off is an mbarrier, tested a step
+// ahead where the answer would otherwise stall the tensor cores, and every wait is bounded
+// by %globaltimer; a timeout raises B2_DEV_PIPE_TIMEOUT and the CTA drains its
 // copies, frees TMEM and returns.  A block id outside the pool raises B2_DEV_RANGE and its
 // keys are read from block 0 and masked (so no uninitialised shared memory is ever used).
 #include <mutex>
@@ -53,21 +54,20 @@ using namespace b2::tc;
 constexpr int HD = 128;
 constexpr int ROWS = 128;                              // MMA M: (token, head) rows per Q tile
 constexpr int KT = 64;                                 // keys per KV tile (4 pool blocks)
-constexpr int ST = 3;                                  // KV ring stages
+constexpr int ST = 4;                                  // KV ring stages
 constexpr int NG = 2;                                  // Q tiles (softmax groups) per item
 constexpr int kGroupWarps = 4;                         // one per TMEM lane quarter
 constexpr int kThreads = 64 + 32 * NG * kGroupWarps;   // producer, MMA, softmax warps
 constexpr uint32_t HALF = KT * 64 * 2;                 // 8 KB: 64 keys x 64 dims
 constexpr uint32_t STAGE = 4 * HALF;                   // K lo | K hi | V lo | V hi
-constexpr uint32_t P_BYTES = ROWS * KT * 2;            // 16 KB: one P tile (two per group)
 constexpr uint32_t Q_HALF = ROWS * 64 * 2;             // 16 KB
 constexpr uint32_t Q_BYTES = 2 * Q_HALF;               // one Q tile, lo | hi
-// Layout (1024-byte aligned): the K/V ring, then P[NG][2], then Q[NG]: 225 KB.
-constexpr uint32_t OFF_P = ST * STAGE;
-constexpr uint32_t OFF_Q = OFF_P + NG * 2 * P_BYTES;
+// Layout (1024-byte aligned): the K/V ring, then Q[NG]: 193 KB.
+constexpr uint32_t OFF_Q = ST * STAGE;
 constexpr size_t SMEM = OFF_Q + NG * Q_BYTES + 1024;
 static_assert(SMEM + 512 <= 232448, "shared memory above the 227 KB a CTA may use");
-// TMEM per group (256 columns): S[2] (64 each) then O (128); 512 in all.
+// TMEM per group (256 columns): S[2] (64 each) then O (128); 512 in all.  P(j) in bf16
+// overwrites the first 32 columns of S(j)'s buffer once the softmax has read S(j).
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t GROUP_COLS = 256, COL_S = 0, COL_O = 128;
 constexpr float kRescale = 8.f;                        // log2 of the largest P before O is rescaled
@@ -103,6 +103,24 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// A barrier phase tested ahead of time (mbar_test) and the answer, consumed by wait_peeked.
+struct Peek {
+  uint32_t addr, parity;
+  bool ok;
+};
+__device__ __forceinline__ void peek(Peek& k, uint64_t* bar, uint32_t parity) {
+  k.addr = smem_u32(bar);
+  k.parity = parity;
+  k.ok = mbar_test(bar, parity);
+}
+// True once the phase of `bar` with `parity` has completed: at once when the last peek saw
+// it complete, else after a bounded wait (false on timeout).
+__device__ __forceinline__ bool wait_peeked(Peek& k, uint64_t* bar, uint32_t parity) {
+  const bool hit = k.ok && k.addr == smem_u32(bar) && k.parity == parity;
+  k.ok = false;
+  return hit || mbar_wait(bar, parity);
 }
 
 // 32 lanes x 32 consecutive 32-bit columns stored to TMEM (the caller waits with
@@ -218,7 +236,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t kv_full[ST];
   __shared__ __align__(8) uint64_t kv_empty[ST];
   __shared__ __align__(8) uint64_t s_full[NG][2];
-  __shared__ __align__(8) uint64_t s_empty[NG][2];
   __shared__ __align__(8) uint64_t p_full[NG][2];
   __shared__ __align__(8) uint64_t pv_done[NG][2];
   __shared__ __align__(8) uint64_t o_empty[NG];
@@ -236,10 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int g = 0; g < NG; ++g) {
       mbar_init(&q_full[g], 1);
       mbar_init(&q_empty[g], 1);
-      for (int b = 0; b < 2; ++b) {
-        mbar_init(&s_full[g][b], 1);
-        mbar_init(&s_empty[g][b], kGroupWarps);
-      }
+      for (int b = 0; b < 2; ++b) mbar_init(&s_full[g][b], 1);
       for (int b = 0; b < 2; ++b) {
         mbar_init(&p_full[g][b], kGroupWarps);
         mbar_init(&pv_done[g][b], 1);
@@ -343,29 +357,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer
+    // The tensor cores queue only about one MMA ahead, so a wait on a barrier that has
+    // already completed (a few hundred cycles for the answer) would leave them idle.  The
+    // barrier of the next step is therefore tested before the current step's MMAs are
+    // issued (peek) and only waited for when that answer was no.  S(n) into S buffer n & 1
+    // needs no barrier of its own: the softmax hands over P(n - 2) only after it has read
+    // S(n - 2), and PV(n - 2) is issued (after that hand-over) before S(n).
     constexpr uint32_t idesc_s = instr_desc_bf16(ROWS, KT);
     constexpr uint32_t idesc_pv = instr_desc_bf16(ROWS, HD) | (1u << 16);  // B (V) MN-major
     int iq[NG] = {0, 0};  // Q tiles consumed per group
-    int js[NG] = {0, 0};  // S tiles issued per group (= PV tiles issued, after each item)
+    int js[NG] = {0, 0};  // S tiles issued per group
     int jp[NG] = {0, 0};  // PV tiles issued per group
     int io[NG] = {0, 0};  // items started per group (O hand-offs)
     int J = 0;
     bool ok = true;
-    // O_g (+)= P_g V of the K/V tile in ring stage `st`; `first` starts the item's O.
-    auto issue_pv = [&](int g, int st, bool first) -> bool {
+    Peek pk_kv{0u, 0u, false}, pk_pf[NG] = {{0u, 0u, false}, {0u, 0u, false}};
+    auto peek_pf = [&](int g) { peek(pk_pf[g], &p_full[g][jp[g] & 1], (uint32_t)(jp[g] >> 1) & 1u); };
+    auto peek_kv = [&](int Jn) { peek(pk_kv, &kv_full[Jn % ST], (uint32_t)(Jn / ST) & 1u); };
+    // O_g (+)= P_g V of the K/V tile in ring stage `st`; `first` starts the item's O; `ahead`
+    // looks at the barrier of the step after this one, before this step's MMAs are issued.
+    auto issue_pv = [&](int g, int st, bool first, auto&& ahead) -> bool {
       const int pb = jp[g] & 1;
-      if (!mbar_wait(&p_full[g][pb], (uint32_t)(jp[g] >> 1) & 1u)) return false;
+      if (!wait_peeked(pk_pf[g], &p_full[g][pb], (uint32_t)(jp[g] >> 1) & 1u)) return false;
       if (first) {  // the previous item's O has been read out of TMEM
         if (!mbar_wait(&o_empty[g], ((uint32_t)io[g] & 1u) ^ 1u)) return false;
         ++io[g];
       }
       tc_fence_after();
-      const uint32_t p_addr = smem_u32(smem + OFF_P + (g * 2 + pb) * P_BYTES);
+      ahead();
+      const uint32_t p_tmem = tmem + g * GROUP_COLS + COL_S + pb * KT;  // P(jp) in S buffer jp & 1
       const uint32_t v_addr = smem_u32(smem + (size_t)st * STAGE + 2 * HALF);
 #pragma unroll
-      for (int kk = 0; kk < KT / 16; ++kk)  // 16 keys per MMA: +32 bytes of P rows, +2 KB of V rows
-        umma_bf16(tmem + g * GROUP_COLS + COL_O, smem_desc_sw128(p_addr) + 2 * kk,
-                  smem_desc_sw128_mn(v_addr + kk * 2048, HALF, 1024), idesc_pv, (first && kk == 0) ? 0u : 1u);
+      for (int kk = 0; kk < KT / 16; ++kk)  // 16 keys per MMA: +8 TMEM columns of P, +2 KB of V rows
+        umma_bf16_ts(tmem + g * GROUP_COLS + COL_O, p_tmem + kk * 8, smem_desc_sw128_mn(v_addr + kk * 2048, HALF, 1024),
+                     idesc_pv, (first && kk == 0) ? 0u : 1u);
       umma_commit(&pv_done[g][pb]);
       ++jp[g];
       return true;
@@ -382,21 +407,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int j = 0; j < it.n_kv[0] && ok; ++j, ++J) {
           const int st = J % ST;
-          if (!mbar_wait(&kv_full[st], (uint32_t)(J / ST) & 1u)) {
+          if (!wait_peeked(pk_kv, &kv_full[st], (uint32_t)(J / ST) & 1u)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t k_addr = smem_u32(smem + (size_t)st * STAGE);
+          const int g_last = j < it.n_kv[1] ? 1 : 0;  // the last S batch of this tile
 #pragma unroll
           for (int g = 0; g < NG; ++g) {
-            if (j >= it.n_kv[g] || !ok) continue;
-            const int b = js[g] & 1;
-            if (!mbar_wait(&s_empty[g][b], ((uint32_t)(js[g] >> 1) & 1u) ^ 1u)) {
-              ok = false;
-              continue;
+            if (j >= it.n_kv[g]) continue;
+            if (g == g_last) {  // next: PV_0 of tile j - 1, or the next K/V tile
+              if (j >= 1) peek_pf(0);
+              else peek_kv(J + 1);
             }
-            tc_fence_after();
+            const int b = js[g] & 1;
             const uint32_t q_addr = smem_u32(smem + OFF_Q + g * Q_BYTES);
 #pragma unroll
             for (int half = 0; half < 2; ++half)
@@ -410,17 +435,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (j >= 1) {
             const int pst = (J - 1) % ST;
-#pragma unroll
-            for (int g = 0; g < NG; ++g)
-              if (ok && j - 1 < it.n_kv[g]) ok = issue_pv(g, pst, j == 1);
+            const bool two = j - 1 < it.n_kv[1];  // group 1 also has a PV of tile j - 1
+            if (ok) ok = issue_pv(0, pst, j == 1, [&] {
+                if (two) peek_pf(1);
+                else peek_kv(J + 1);
+              });
+            if (ok && two) ok = issue_pv(1, pst, j == 1, [&] { peek_kv(J + 1); });
             umma_commit(&kv_empty[pst]);  // both groups' S and PV of tile j - 1 have been issued
           }
         }
-        if (ok && it.n_kv[0] > 0) {  // the item's last tile
+        if (ok && it.n_kv[0] > 0) {  // the item's last tile (J is already the next tile's index)
           const int pst = (J - 1) % ST;
-#pragma unroll
-          for (int g = 0; g < NG; ++g)
-            if (ok && it.n_kv[g] == it.n_kv[0]) ok = issue_pv(g, pst, it.n_kv[0] == 1);
+          const bool two = it.n_kv[1] == it.n_kv[0];
+          const bool first = it.n_kv[0] == 1;
+          ok = issue_pv(0, pst, first, [&] {
+            if (two) peek_pf(1);
+            else peek_kv(J);
+          });
+          if (ok && two) ok = issue_pv(1, pst, first, [&] { peek_kv(J); });
           umma_commit(&kv_empty[pst]);
         }
         if (!ok) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
@@ -442,6 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tk = m / REP, h = m % REP;
     int js = 0;  // S tiles consumed by this group (the PV of tile js - 1 is the latest issued)
     bool ok = true;
+    Peek pk_s{0u, 0u, false};  // the next S tile, tested while this tile's P is written
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
       const Item it = find_item<QT>(p, w, lane);
       // this group's tile (selected without indexing, so the item stays in registers)
@@ -455,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < n_kv; ++j, ++js) {
         const int b = js & 1;
         // warp-uniform verdicts: the TMEM loads and stores below are .sync.aligned
-        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[grp][b], (uint32_t)(js >> 1) & 1u))) {
+        if (!__all_sync(0xffffffffu, wait_peeked(pk_s, &s_full[grp][b], (uint32_t)(js >> 1) & 1u))) {
           ok = false;
           break;
         }
@@ -464,9 +497,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32_nowait(trow + COL_S + b * KT, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
         tmem_ld32_nowait(trow + COL_S + b * KT + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
         tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_empty[grp][b]);  // the S buffer may be rewritten
         // raw scores; masked keys are -inf (scale_log2 > 0, so the maximum commutes with it)
         const int k0 = j * KT;
         float sv[64];
@@ -477,12 +507,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 64; ++e) sv[e] = (row_ok && k0 + e <= pos) ? __uint_as_float(sr[e]) : -INFINITY;
         }
-        float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
+        float mx8[8];
 #pragma unroll
-        for (int e = 4; e < 64; e += 4)
+        for (int u = 0; u < 8; ++u) mx8[u] = sv[u];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) mx4[u] = fmaxf(mx4[u], sv[e + u]);
-        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
+        for (int e = 8; e < 64; e += 8)
+#pragma unroll
+          for (int u = 0; u < 8; ++u) mx8[u] = fmaxf(mx8[u], sv[e + u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mx8[u] = fmaxf(mx8[u], mx8[u + 4]);
+        const float mx = fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])) * p.scale_log2;
         // the reference maximum: set by the first visible key, raised only by more than kRescale
         bool need = false;
         float corr = 1.f;
@@ -491,11 +525,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (mx > m_ref + kRescale) {
           need = true;
           corr = exp2f(m_ref - mx);
-        }
-        // P buffer b was last read by PV(js - 2), normally long complete
-        if (js >= 2 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[grp][b], (uint32_t)((js - 2) >> 1) & 1u))) {
-          ok = false;
-          break;
         }
         if (__any_sync(0xffffffffu, need)) {
           // O must hold PV(js - 1) before it is rescaled (need implies j >= 1)
@@ -522,11 +551,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // P = exp2(s * scale_log2 - m_ref) in bf16 into the swizzled row of the group's P tile;
         // a row with nothing visible keeps p = 0 (m_ref = -inf is replaced by 0)
         const float m_sub = m_ref == -INFINITY ? 0.f : m_ref;
-        uint8_t* prow = smem + OFF_P + (grp * 2 + b) * P_BYTES + m * 128;
         float ls[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t pw[32];  // the row's P in bf16 pairs: word w holds keys 2w (low half) and 2w + 1
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          uint32_t wv[4];
+          // the next S tile this group consumes (in this item or the next): ask now, so that the
+          // answer has arrived when this tile is done
+          if (q == 2) peek(pk_s, &s_full[grp][(js + 1) & 1], (uint32_t)((js + 1) >> 1) & 1u);
 #pragma unroll
           for (int e2 = 0; e2 < 4; ++e2) {
             const int e = q * 8 + e2 * 2;
@@ -534,13 +565,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float p1 = ex2_approx(fmaf(sv[e + 1], p.scale_log2, -m_sub));
             ls[e2] += p0 + p1;
             __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-            wv[e2] = *reinterpret_cast<uint32_t*>(&h2);
+            pw[q * 4 + e2] = *reinterpret_cast<uint32_t*>(&h2);
           }
-          *reinterpret_cast<uint4*>(prow + ((q ^ (m & 7)) << 4)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
         l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-        fence_proxy_async_smem();  // P written by these threads is read by the tensor cores
-        tc_fence_before();         // and so are the rescaled O columns
+        // P over the first 32 columns of this S buffer (read above): the A operand of PV(js),
+        // which the tensor cores run before S(js + 2) rewrites the buffer
+        tmem_st32(trow + COL_S + b * KT, pw);
+        tmem_wait_st();
+        tc_fence_before();  // P and the rescaled O columns are read by the tensor cores
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[grp][b]);
       }
