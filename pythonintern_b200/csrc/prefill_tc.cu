@@ -54,7 +54,7 @@ using namespace b2::tc;
 constexpr int HD = 128;
 constexpr int ROWS = 128;                              // MMA M: (token, head) rows per Q tile
 constexpr int KT = 64;                                 // keys per KV tile (4 pool blocks)
-constexpr int ST = 4;                                  // KV ring stages
+constexpr int ST = 3;                                  // KV ring stages
 constexpr int NG = 2;                                  // Q tiles (softmax groups) per item
 constexpr int kGroupWarps = 4;                         // one per TMEM lane quarter
 constexpr int kThreads = 64 + 32 * NG * kGroupWarps;   // producer, MMA, softmax warps
@@ -62,9 +62,10 @@ constexpr uint32_t HALF = KT * 64 * 2;                 // 8 KB: 64 keys x 64 dim
 constexpr uint32_t STAGE = 4 * HALF;                   // K lo | K hi | V lo | V hi
 constexpr uint32_t Q_HALF = ROWS * 64 * 2;             // 16 KB
 constexpr uint32_t Q_BYTES = 2 * Q_HALF;               // one Q tile, lo | hi
-// Layout (1024-byte aligned): the K/V ring, then Q[NG]: 193 KB.
+// Layout (1024-byte aligned): the K/V ring, then Q[NG][2] (the next item's Q tiles load
+// while this item runs): 225 KB.
 constexpr uint32_t OFF_Q = ST * STAGE;
-constexpr size_t SMEM = OFF_Q + NG * Q_BYTES + 1024;
+constexpr size_t SMEM = OFF_Q + NG * 2 * Q_BYTES + 1024;
 static_assert(SMEM + 512 <= 232448, "shared memory above the 227 KB a CTA may use");
 // TMEM per group (256 columns): S[2] (64 each) then O (128); 512 in all.  P(j) in bf16
 // overwrites the first 32 columns of S(j)'s buffer once the softmax has read S(j).
@@ -231,8 +232,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                            const __grid_constant__ CUtensorMap tmV, const Params p) {
   constexpr int QT = ROWS / REP;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full[NG];
-  __shared__ __align__(8) uint64_t q_empty[NG];
+  __shared__ __align__(8) uint64_t q_full[NG][2];
+  __shared__ __align__(8) uint64_t q_empty[NG][2];
   __shared__ __align__(8) uint64_t kv_full[ST];
   __shared__ __align__(8) uint64_t kv_empty[ST];
   __shared__ __align__(8) uint64_t s_full[NG][2];
@@ -251,8 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int g = 0; g < NG; ++g) {
-      mbar_init(&q_full[g], 1);
-      mbar_init(&q_empty[g], 1);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&q_full[g][b], 1);
+        mbar_init(&q_empty[g][b], 1);
+      }
       for (int b = 0; b < 2; ++b) mbar_init(&s_full[g][b], 1);
       for (int b = 0; b < 2; ++b) {
         mbar_init(&p_full[g][b], kGroupWarps);
@@ -290,15 +293,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int g = 0; g < NG; ++g) {
           if (it.nt[g] == 0 || !ok) continue;
-          if (!mbar_wait(&q_empty[g], ((uint32_t)iq[g] & 1u) ^ 1u)) {
+          const int qb = iq[g] & 1;
+          if (!mbar_wait(&q_empty[g][qb], ((uint32_t)(iq[g] >> 1) & 1u) ^ 1u)) {
             raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
             ok = false;
             continue;
           }
-          uint8_t* qs = smem + OFF_Q + g * Q_BYTES;
-          mbar_arrive_expect_tx(&q_full[g], Q_BYTES);
-          tma_load_3d(qs, &tmQ, &q_full[g], 0, it.g * REP, it.rs + it.t0[g], pol_q);
-          tma_load_3d(qs + Q_HALF, &tmQ, &q_full[g], 64, it.g * REP, it.rs + it.t0[g], pol_q);
+          uint8_t* qs = smem + OFF_Q + (g * 2 + qb) * Q_BYTES;
+          mbar_arrive_expect_tx(&q_full[g][qb], Q_BYTES);
+          tma_load_3d(qs, &tmQ, &q_full[g][qb], 0, it.g * REP, it.rs + it.t0[g], pol_q);
+          tma_load_3d(qs + Q_HALF, &tmQ, &q_full[g][qb], 64, it.g * REP, it.rs + it.t0[g], pol_q);
           ++iq[g];
         }
       }
@@ -348,7 +352,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // Copies still in flight (only after an aborted pipeline) land before the CTA exits.
       for (int g = 0; g < NG; ++g)
-        if (iq[g] > 0) mbar_wait(&q_full[g], (uint32_t)(iq[g] - 1) & 1u, 100000000ull);
+        for (int qb = 0; qb < 2; ++qb) {
+          const int loads = (iq[g] + 1 - qb) / 2;  // copies made into buffer qb of group g
+          if (loads > 0) mbar_wait(&q_full[g][qb], (uint32_t)(loads - 1) & 1u, 100000000ull);
+        }
       for (int st = 0; st < ST && st < J; ++st) {
         const int last_i = st + ((J - 1 - st) / ST) * ST;
         mbar_wait(&kv_full[st], (uint32_t)(last_i / ST) & 1u, 100000000ull);
@@ -357,18 +364,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer
-    // The tensor cores queue only about one MMA ahead, so a wait on a barrier that has
-    // already completed (a few hundred cycles for the answer) would leave them idle.  The
-    // barrier of the next step is therefore tested before the current step's MMAs are
-    // issued (peek) and only waited for when that answer was no.  S(n) into S buffer n & 1
-    // needs no barrier of its own: the softmax hands over P(n - 2) only after it has read
-    // S(n - 2), and PV(n - 2) is issued (after that hand-over) before S(n).
+    // The whole warp runs this control code, so that the operand descriptors stay in uniform
+    // registers; one elected lane issues every tcgen05.mma and tcgen05.commit.  The tensor
+    // cores queue only about one MMA ahead, so a wait on a barrier that has already completed
+    // (a few hundred cycles for the answer) would leave them idle: the barrier of the next
+    // step is tested before the current step's MMAs are issued (peek) and only waited for
+    // when that answer was no.  S(n) into S buffer n & 1 needs no barrier of its own: the
+    // softmax hands over P(n - 2) only after it has read S(n - 2), and PV(n - 2) is issued
+    // (after that hand-over) before S(n).
     constexpr uint32_t idesc_s = instr_desc_bf16(ROWS, KT);
     constexpr uint32_t idesc_pv = instr_desc_bf16(ROWS, HD) | (1u << 16);  // B (V) MN-major
     int iq[NG] = {0, 0};  // Q tiles consumed per group
     int js[NG] = {0, 0};  // S tiles issued per group
     int jp[NG] = {0, 0};  // PV tiles issued per group
     int io[NG] = {0, 0};  // items started per group (O hand-offs)
+    int qb[NG] = {0, 0};  // the Q buffer of the current item, per group
     int J = 0;
     bool ok = true;
     Peek pk_kv{0u, 0u, false}, pk_pf[NG] = {{0u, 0u, false}, {0u, 0u, false}};
@@ -378,9 +388,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // looks at the barrier of the step after this one, before this step's MMAs are issued.
     auto issue_pv = [&](int g, int st, bool first, auto&& ahead) -> bool {
       const int pb = jp[g] & 1;
-      if (!wait_peeked(pk_pf[g], &p_full[g][pb], (uint32_t)(jp[g] >> 1) & 1u)) return false;
+      if (!__all_sync(0xffffffffu, wait_peeked(pk_pf[g], &p_full[g][pb], (uint32_t)(jp[g] >> 1) & 1u))) return false;
       if (first) {  // the previous item's O has been read out of TMEM
-        if (!mbar_wait(&o_empty[g], ((uint32_t)io[g] & 1u) ^ 1u)) return false;
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_empty[g], ((uint32_t)io[g] & 1u) ^ 1u))) return false;
         ++io[g];
       }
       tc_fence_after();
@@ -389,80 +399,81 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t v_addr = smem_u32(smem + (size_t)st * STAGE + 2 * HALF);
 #pragma unroll
       for (int kk = 0; kk < KT / 16; ++kk)  // 16 keys per MMA: +8 TMEM columns of P, +2 KB of V rows
-        umma_bf16_ts(tmem + g * GROUP_COLS + COL_O, p_tmem + kk * 8, smem_desc_sw128_mn(v_addr + kk * 2048, HALF, 1024),
-                     idesc_pv, (first && kk == 0) ? 0u : 1u);
-      umma_commit(&pv_done[g][pb]);
+        if (elect_one())
+          umma_bf16_ts(tmem + g * GROUP_COLS + COL_O, p_tmem + kk * 8,
+                       smem_desc_sw128_mn(v_addr + kk * 2048, HALF, 1024), idesc_pv, (first && kk == 0) ? 0u : 1u);
+      if (elect_one()) umma_commit(&pv_done[g][pb]);
       ++jp[g];
       return true;
     };
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
       const Item it = find_item<QT>(p, w, lane);
       if (!it.valid) continue;
-      if (lane == 0) {
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        if (it.nt[g] == 0 || !ok) continue;
+        qb[g] = iq[g] & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&q_full[g][qb[g]], (uint32_t)(iq[g] >> 1) & 1u))) ok = false;
+        ++iq[g];
+      }
+      for (int j = 0; j < it.n_kv[0] && ok; ++j, ++J) {
+        const int st = J % ST;
+        if (!__all_sync(0xffffffffu, wait_peeked(pk_kv, &kv_full[st], (uint32_t)(J / ST) & 1u))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + (size_t)st * STAGE);
+        const int g_last = j < it.n_kv[1] ? 1 : 0;  // the last S batch of this tile
 #pragma unroll
         for (int g = 0; g < NG; ++g) {
-          if (it.nt[g] == 0 || !ok) continue;
-          if (!mbar_wait(&q_full[g], (uint32_t)iq[g] & 1u)) ok = false;
-          ++iq[g];
-        }
-        for (int j = 0; j < it.n_kv[0] && ok; ++j, ++J) {
-          const int st = J % ST;
-          if (!wait_peeked(pk_kv, &kv_full[st], (uint32_t)(J / ST) & 1u)) {
-            ok = false;
-            break;
+          if (j >= it.n_kv[g]) continue;
+          if (g == g_last) {  // next: PV_0 of tile j - 1, or the next K/V tile
+            if (j >= 1) peek_pf(0);
+            else peek_kv(J + 1);
           }
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(smem + (size_t)st * STAGE);
-          const int g_last = j < it.n_kv[1] ? 1 : 0;  // the last S batch of this tile
+          const int b = js[g] & 1;
+          const uint32_t q_addr = smem_u32(smem + OFF_Q + (g * 2 + qb[g]) * Q_BYTES);
 #pragma unroll
-          for (int g = 0; g < NG; ++g) {
-            if (j >= it.n_kv[g]) continue;
-            if (g == g_last) {  // next: PV_0 of tile j - 1, or the next K/V tile
-              if (j >= 1) peek_pf(0);
-              else peek_kv(J + 1);
-            }
-            const int b = js[g] & 1;
-            const uint32_t q_addr = smem_u32(smem + OFF_Q + g * Q_BYTES);
+          for (int half = 0; half < 2; ++half)
 #pragma unroll
-            for (int half = 0; half < 2; ++half)
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
+            for (int kk = 0; kk < 4; ++kk)
+              if (elect_one())
                 umma_bf16(tmem + g * GROUP_COLS + COL_S + b * KT, smem_desc_sw128(q_addr + half * Q_HALF) + 2 * kk,
                           smem_desc_sw128(k_addr + half * HALF) + 2 * kk, idesc_s, (half | kk) ? 1u : 0u);
-            umma_commit(&s_full[g][b]);
-            ++js[g];
-            if (j == it.n_kv[g] - 1) umma_commit(&q_empty[g]);  // every S MMA of this tile has read Q_g
-          }
-          if (j >= 1) {
-            const int pst = (J - 1) % ST;
-            const bool two = j - 1 < it.n_kv[1];  // group 1 also has a PV of tile j - 1
-            if (ok) ok = issue_pv(0, pst, j == 1, [&] {
-                if (two) peek_pf(1);
-                else peek_kv(J + 1);
-              });
-            if (ok && two) ok = issue_pv(1, pst, j == 1, [&] { peek_kv(J + 1); });
-            umma_commit(&kv_empty[pst]);  // both groups' S and PV of tile j - 1 have been issued
+          if (elect_one()) umma_commit(&s_full[g][b]);
+          ++js[g];
+          if (j == it.n_kv[g] - 1) {  // every S MMA of this item has read Q_g
+            if (elect_one()) umma_commit(&q_empty[g][qb[g]]);
           }
         }
-        if (ok && it.n_kv[0] > 0) {  // the item's last tile (J is already the next tile's index)
+        if (j >= 1) {
           const int pst = (J - 1) % ST;
-          const bool two = it.n_kv[1] == it.n_kv[0];
-          const bool first = it.n_kv[0] == 1;
-          ok = issue_pv(0, pst, first, [&] {
-            if (two) peek_pf(1);
-            else peek_kv(J);
-          });
-          if (ok && two) ok = issue_pv(1, pst, first, [&] { peek_kv(J); });
-          umma_commit(&kv_empty[pst]);
+          const bool two = j - 1 < it.n_kv[1];  // group 1 also has a PV of tile j - 1
+          if (ok) ok = issue_pv(0, pst, j == 1, [&] {
+              if (two) peek_pf(1);
+              else peek_kv(J + 1);
+            });
+          if (ok && two) ok = issue_pv(1, pst, j == 1, [&] { peek_kv(J + 1); });
+          if (elect_one()) umma_commit(&kv_empty[pst]);  // both groups' S and PV of tile j - 1 are issued
         }
-        if (!ok) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (ok && it.n_kv[0] > 0) {  // the item's last tile (J is already the next tile's index)
+        const int pst = (J - 1) % ST;
+        const bool two = it.n_kv[1] == it.n_kv[0];
+        const bool first = it.n_kv[0] == 1;
+        ok = issue_pv(0, pst, first, [&] {
+          if (two) peek_pf(1);
+          else peek_kv(J);
+        });
+        if (ok && two) ok = issue_pv(1, pst, first, [&] { peek_kv(J); });
+        if (elect_one()) umma_commit(&kv_empty[pst]);
+      }
+      if (!ok && lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
     }
-    if (lane == 0) {
-      umma_commit(&drain_bar);  // every MMA issued by this thread has completed once it fires
-      mbar_wait(&drain_bar, 0, 100000000ull);
-    }
+    // every MMA issued by the elected lane has completed once drain_bar fires
+    if (elect_one()) umma_commit(&drain_bar);
+    mbar_wait(&drain_bar, 0, 100000000ull);
     __syncwarp();
   } else {
     // ---------------- softmax: one thread per MMA row of its group's Q tile

@@ -188,6 +188,19 @@ __host__ __device__ constexpr uint32_t instr_desc_bf16(int m, int n) {
          | ((uint32_t)(m >> 4) << 24);    // M / 16
 }
 
+// True in exactly one lane of a fully active warp (elect.sync over all 32 lanes, which
+// elects the same leader every time): that lane issues the single-thread tcgen05.mma and
+// tcgen05.commit instructions while the whole warp runs the surrounding control code, so
+// the shared operand descriptors stay in uniform registers.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r));
+  return r != 0;
+}
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
