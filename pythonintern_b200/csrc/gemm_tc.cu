@@ -275,52 +275,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------- MMA issuer (one lane)
-    if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc_bf16(BM, BN);
-      int it = 0, j = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++j) {
-        const Unit w = decode_unit(p, u);
-        const int buf = j % NBUF;
-        const uint32_t acc = tmem + (uint32_t)(buf * C::ACC_COLS);
-        if (!mbar_wait(&acc_empty[buf], ((uint32_t)(j / NBUF) & 1u) ^ 1u)) {
-          raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+    // ---------------- MMA issuer: the whole warp runs the control code (the descriptors stay
+    // in uniform registers), one elected lane issues.  The tensor cores queue only about one
+    // MMA ahead, so the next stage's barrier is tested while this stage's MMAs go out
+    // (peek), and its wait costs nothing when the copy has already landed.
+    constexpr uint32_t idesc = instr_desc_bf16(BM, BN);
+    int it = 0, j = 0;
+    bool ok = true;
+    Peek pk{0u, 0u, false};
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++j) {
+      const Unit w = decode_unit(p, u);
+      const int buf = j % NBUF;
+      const uint32_t acc = tmem + (uint32_t)(buf * C::ACC_COLS);
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], ((uint32_t)(j / NBUF) & 1u) ^ 1u))) {
+        if (lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+        break;
+      }
+      tc_fence_after();
+      const int kb0 = w.split * p.kb_per_split;
+      const int kb1 = min(p.nkb, kb0 + p.kb_per_split);
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int st = it % STAGES;
+        const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+        if (!__all_sync(0xffffffffu, wait_peeked(pk, &full_bar[st], ph))) {
+          if (lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+          ok = false;
           break;
         }
         tc_fence_after();
-        const int kb0 = w.split * p.kb_per_split;
-        const int kb1 = min(p.nkb, kb0 + p.kb_per_split);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int st = it % STAGES;
-          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-          if (!mbar_wait(&full_bar[st], ph)) {
-            raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + (size_t)st * C::STAGE_BYTES);
-          const uint64_t adesc = smem_desc_sw128(a_addr);
-          const uint64_t bdesc = smem_desc_sw128(a_addr + C::A_BYTES);
-          const uint32_t first = kb == kb0 ? 1u : 0u;
+        const uint32_t a_addr = smem_u32(smem + (size_t)st * C::STAGE_BYTES);
+        const uint64_t adesc = smem_desc_sw128(a_addr);
+        const uint64_t bdesc = smem_desc_sw128(a_addr + C::A_BYTES);
+        const uint32_t first = kb == kb0 ? 1u : 0u;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)  // +32 bytes along K per MMA = +2 in the address field
-            umma_bf16(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
-          if (SWIGLU) {
-            const uint64_t udesc = smem_desc_sw128(a_addr + BM * BK * 2);
-#pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk)
-              umma_bf16(acc + BN, udesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
-          }
-          umma_commit(&empty_bar[st]);
+        for (int kk = 0; kk < BK / 16; ++kk) {  // +32 bytes along K per MMA = +2 in the address field
+          if (elect_one()) umma_bf16(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
+          if (kk == 0)  // the next stage (of this unit or the next), while this one's MMAs run
+            peek(pk, &full_bar[(it + 1) % STAGES], (uint32_t)((it + 1) / STAGES) & 1u);
         }
-        umma_commit(&acc_full[buf]);
+        if (SWIGLU) {
+          const uint64_t udesc = smem_desc_sw128(a_addr + BM * BK * 2);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            if (elect_one()) umma_bf16(acc + BN, udesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
+        }
+        if (elect_one()) umma_commit(&empty_bar[st]);
       }
-      // Every MMA issued by this thread has completed once drain_bar fires.
-      umma_commit(&drain_bar);
-      mbar_wait(&drain_bar, 0, 100000000ull);
+      if (elect_one()) umma_commit(&acc_full[buf]);
     }
+    // Every MMA issued by the elected lane has completed once drain_bar fires.
+    if (elect_one()) umma_commit(&drain_bar);
+    mbar_wait(&drain_bar, 0, 100000000ull);
     __syncwarp();
   } else {
     // ---------------- epilogue warps 2-5
@@ -571,34 +576,37 @@ __global__ void __launch_bounds__(kThreadsCl, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc_bf16(BM, BN);
-      int it = 0;
-      for (int kb = kb0; kb < kb1; ++kb, ++it) {
-        const int st = it % STAGES;
-        const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-        if (!mbar_wait(&full_bar[st], ph)) {
-          raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
-          break;
-        }
-        tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + (size_t)st * C::STAGE_BYTES);
-        const uint64_t adesc = smem_desc_sw128(a_addr);
-        const uint64_t bdesc = smem_desc_sw128(a_addr + C::A_BYTES);
-        const uint32_t first = kb == kb0 ? 1u : 0u;
+    // MMA issuer: warp-uniform control code, one elected lane issues, the next stage's
+    // barrier tested while this stage's MMAs go out (as in gemm_tc_kernel).
+    constexpr uint32_t idesc = instr_desc_bf16(BM, BN);
+    int it = 0;
+    Peek pk{0u, 0u, false};
+    for (int kb = kb0; kb < kb1; ++kb, ++it) {
+      const int st = it % STAGES;
+      const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+      if (!__all_sync(0xffffffffu, wait_peeked(pk, &full_bar[st], ph))) {
+        if (lane == 0) raise_status(p.status, B2_DEV_PIPE_TIMEOUT);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t a_addr = smem_u32(smem + (size_t)st * C::STAGE_BYTES);
+      const uint64_t adesc = smem_desc_sw128(a_addr);
+      const uint64_t bdesc = smem_desc_sw128(a_addr + C::A_BYTES);
+      const uint32_t first = kb == kb0 ? 1u : 0u;
+#pragma unroll
+      for (int kk = 0; kk < BK / 16; ++kk) {
+        if (elect_one()) umma_bf16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
+        if (kk == 0 && kb + 1 < kb1) peek(pk, &full_bar[(it + 1) % STAGES], (uint32_t)((it + 1) / STAGES) & 1u);
+      }
+      if (SWIGLU) {
+        const uint64_t udesc = smem_desc_sw128(a_addr + BM * BK * 2);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
-          umma_bf16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
-        if (SWIGLU) {
-          const uint64_t udesc = smem_desc_sw128(a_addr + BM * BK * 2);
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            umma_bf16(tmem + BN, udesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
-        }
-        umma_commit(&empty_bar[st]);
+          if (elect_one()) umma_bf16(tmem + BN, udesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
       }
-      umma_commit(&acc_full);
+      if (elect_one()) umma_commit(&empty_bar[st]);
     }
+    if (elect_one()) umma_commit(&acc_full);
     __syncwarp();
   }
 

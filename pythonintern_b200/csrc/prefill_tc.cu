@@ -106,24 +106,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// A barrier phase tested ahead of time (mbar_test) and the answer, consumed by wait_peeked.
-struct Peek {
-  uint32_t addr, parity;
-  bool ok;
-};
-__device__ __forceinline__ void peek(Peek& k, uint64_t* bar, uint32_t parity) {
-  k.addr = smem_u32(bar);
-  k.parity = parity;
-  k.ok = mbar_test(bar, parity);
-}
-// True once the phase of `bar` with `parity` has completed: at once when the last peek saw
-// it complete, else after a bounded wait (false on timeout).
-__device__ __forceinline__ bool wait_peeked(Peek& k, uint64_t* bar, uint32_t parity) {
-  const bool hit = k.ok && k.addr == smem_u32(bar) && k.parity == parity;
-  k.ok = false;
-  return hit || mbar_wait(bar, parity);
-}
-
 // 32 lanes x 32 consecutive 32-bit columns stored to TMEM (the caller waits with
 // tmem_wait_st() before the tensor cores may read them).
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {

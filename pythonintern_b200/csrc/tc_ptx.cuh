@@ -58,6 +58,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
     if ((i & 63) == 0 && globaltimer_ns() - t0 > bound_ns) return false;
   }
 }
+// A barrier phase tested ahead of time (mbar_test) and the answer, consumed by wait_peeked.
+struct Peek {
+  uint32_t addr, parity;
+  bool ok;
+};
+__device__ __forceinline__ void peek(Peek& k, uint64_t* bar, uint32_t parity) {
+  k.addr = smem_u32(bar);
+  k.parity = parity;
+  k.ok = mbar_test(bar, parity);
+}
+// True once the phase of `bar` with `parity` has completed: at once when the last peek saw
+// it complete, else after a bounded wait (false on timeout).
+__device__ __forceinline__ bool wait_peeked(Peek& k, uint64_t* bar, uint32_t parity) {
+  const bool hit = k.ok && k.addr == smem_u32(bar) && k.parity == parity;
+  k.ok = false;
+  return hit || mbar_wait(bar, parity);
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
                                             uint64_t policy) {
   asm volatile(
