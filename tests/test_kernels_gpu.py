@@ -152,7 +152,10 @@ def test_linear_qkv(dtype, M):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("M,N,K", [(1, 344, 256), (8, 2816, 2048), (128, 1792, 4096), (70, 200, 256),
-                                   (128, 14336, 4096), (16, 12288, 1024), (300, 2816, 2048), (1000, 1792, 1024)])
+                                   (128, 14336, 4096), (16, 12288, 1024), (300, 2816, 2048), (1000, 1792, 1024),
+                                   # 74..147 tiles of 128 rows: one shorter tile per SM (97, 88, 68 rows;
+                                   # the last tile of the two ragged shapes is partial)
+                                   (128, 13000, 1024), (40, 10000, 512)])
 def test_linear_swiglu(dtype, M, N, K):
     x = torch.randn(M, K, generator=g(M)).to(DEV, dtype)
     wg = (torch.randn(N, K, generator=g(1)) / math.sqrt(K)).to(DEV, dtype)
