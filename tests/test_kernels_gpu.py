@@ -108,6 +108,9 @@ def test_linear_float32(M, N, K):
     (128, 6144, 4096), (129, 256, 256), (200, 384, 320), (300, 640, 2048), (1, 4096, 14336),
     (128, 14336, 4096), (100, 12800, 1024), (64, 10240, 2048),  # 74..147 tiles: one wave, idle SMs
     (240, 768, 4096), (240, 4096, 14336), (512, 4096, 7168), (513, 512, 1024),  # 128-wide token tiles to 512
+    # the 8B layer's GEMMs at eight ranks: q|k|v 768 x 4096 (split-K 8, one k block per stage
+    # set), o_proj 4096 x 512 (two k blocks per split), down 4096 x 1792
+    (128, 768, 4096), (128, 4096, 512), (128, 4096, 1792), (8, 4096, 512),
 ])
 def test_linear_bf16_tensor_cores(M, N, K):
     """tcgen05 GEMM (swap-AB, split-K where chosen) against the float64 oracle on the same bf16 inputs."""
